@@ -1,0 +1,119 @@
+/*
+ * samrs_b200.h - C ABI of the B200 (sm_100a) decomposed-rel-pos attention library.
+ *
+ * The entry points replace the device side of the candle custom ops that sam-rs uses for the
+ * attention of its SAM ViT image encoder (reference: apiplant/sam-rs 0.1.1):
+ *
+ *   samrs_relpos_attn_fwd    <- src/kernels.rs:896-906  `attention_relpos_cpu(q, kt, v, table, h, w, scale)`
+ *                               (the fused op; on CUDA the reference instead runs
+ *                               src/sam1/encoder.rs:81 `bmm(relpos_softmax(bmm(q, kt)), v)`)
+ *   samrs_relpos_softmax_fwd <- src/kernels.rs:12-43   `relpos_softmax(scores, q, table, h, w, scale)`
+ *                               and its CUDA launcher src/kernels.rs:1108-1149 (kernels/sam.cu:44-106)
+ *   samrs_qkv_split_fwd      <- src/kernels.rs:870-894 `qkv_split(y, bias, n, nh, hd)`
+ *                               and its CUDA launcher src/kernels.rs:1196-1227 (kernels/sam.cu:108-128)
+ *
+ * Conventions shared by every entry point
+ *  - All tensors are dense, contiguous, row-major device buffers owned by the caller
+ *    (candle allocates them with `dev.alloc`, src/kernels.rs:1124). Nothing here allocates
+ *    device memory, synchronises the stream or keeps per-call host state.
+ *  - `dtype`: SAMRS_F32 / SAMRS_F16 / SAMRS_BF16, the same three candle dtypes the reference
+ *    dispatches on (src/kernels.rs:1086-1095). All tensors of one call share the dtype.
+ *  - `stream`: a `cudaStream_t` (cudarc's stream handle in candle); NULL = legacy default stream.
+ *    Work is enqueued asynchronously on it.
+ *  - Return value: SAMRS_OK (0) or a negative error code; `samrs_last_error()` then returns a
+ *    message for the calling thread (the reference's `bail!` text, src/kernels.rs:1092,1097-1102).
+ *  - Layouts (bh = window * nh + head, exactly as `qkv_split` produces them, src/kernels.rs:880-882):
+ *        q     [bh, h*w, hd]
+ *        kt    [bh, hd, h*w]       (K already transposed)
+ *        v     [bh, h*w, hd]
+ *        table [(2h-1) + (2w-1), hd]   rel_pos_h rows then rel_pos_w rows (src/sam1/encoder.rs:56-69)
+ *        out   [bh, h*w, hd]
+ */
+#ifndef SAMRS_B200_H
+#define SAMRS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SAMRS_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define SAMRS_API __attribute__((visibility("default")))
+#else
+#define SAMRS_API
+#endif
+
+/* dtype codes */
+#define SAMRS_F32 0
+#define SAMRS_F16 1
+#define SAMRS_BF16 2
+
+/* return codes */
+#define SAMRS_OK 0
+#define SAMRS_ERR_INVALID (-1)     /* bad shape, dtype, null or misaligned pointer        */
+#define SAMRS_ERR_UNSUPPORTED (-2) /* shape outside every kernel's range                   */
+#define SAMRS_ERR_LAUNCH (-3)      /* CUDA launch / attribute error                         */
+#define SAMRS_ERR_DEVICE (-4)      /* a kernel reported a fault in the device status word   */
+#define SAMRS_ERR_NODEVICE (-5)    /* no sm_100 device is current                           */
+
+/* implementation selector for samrs_relpos_attn_fwd_ex */
+#define SAMRS_IMPL_AUTO 0  /* tensor-core kernels where the shape allows, SIMT kernel otherwise */
+#define SAMRS_IMPL_SIMT 1  /* CUDA-core fused flash kernel (any shape, any dtype)               */
+#define SAMRS_IMPL_TC 2    /* tcgen05 kernels only; SAMRS_ERR_UNSUPPORTED if the shape does not fit */
+
+/*
+ * Fused attention with decomposed relative-position bias, one pass, no N x N tensor in memory:
+ *   out[b, r, :] = sum_k softmax_k( scale * q[b,r,:].kt[b,:,k] + q[b,r,:].Th[i-kh+h-1] + q[b,r,:].Tw[j-kw+w-1] ) v[b,k,:]
+ *   with r = i*w + j, k = kh*w + kw, Th = table[0 : 2h-1], Tw = table[2h-1 : 2h-1+2w-1].
+ * Replaces src/kernels.rs:896-906 (`attention_relpos_cpu`, whose f32 CPU body is
+ * src/kernels.rs:131-225 `cpu::TiledAttention`). Limits: 1 <= h, w <= 128, 1 <= hd <= 128,
+ * bh >= 0 (bh == 0 is a no-op). Pointers must be aligned to the element size; the tensor-core
+ * path additionally wants 16-byte aligned q, v, out (it falls back to the SIMT kernel otherwise).
+ */
+SAMRS_API int samrs_relpos_attn_fwd(const void* q, const void* kt, const void* v, const void* table, void* out,
+                          int64_t bh, int h, int w, int hd, float scale, int dtype, void* stream);
+
+/* Same as samrs_relpos_attn_fwd with an explicit implementation choice (SAMRS_IMPL_*). */
+SAMRS_API int samrs_relpos_attn_fwd_ex(const void* q, const void* kt, const void* v, const void* table, void* out,
+                             int64_t bh, int h, int w, int hd, float scale, int dtype, int impl, void* stream);
+
+/*
+ * Materialising rel-pos softmax (the reference's `relpos_softmax`, src/kernels.rs:12-43, CUDA
+ * kernel kernels/sam.cu:44-106):
+ *   out[row, kh*w+kw] = softmax( scale*s[row, k] + q[row,:].Th[i-kh+h-1] + q[row,:].Tw[j-kw+w-1] )
+ *   s, out: [rows, h*w]; q: [rows, hd]; row % (h*w) = i*w + j. rows = bh*h*w.
+ * Limits: as samrs_relpos_attn_fwd, plus h*w <= 16384.
+ */
+SAMRS_API int samrs_relpos_softmax_fwd(const void* s, const void* q, const void* table, void* out, int64_t rows,
+                             int h, int w, int hd, float scale, int dtype, void* stream);
+
+/*
+ * QKV head split (the reference's `qkv_split`, src/kernels.rs:870-894, kernels/sam.cu:108-128):
+ *   y [tokens, 3*nh*hd] (+ bias [3*nh*hd]) -> out = [q | kt | v], each tokens*nh*hd elements,
+ *   q, v: [bh, n, hd], kt: [bh, hd, n], bh = (tokens / n) * nh. tokens must be a multiple of n.
+ */
+SAMRS_API int samrs_qkv_split_fwd(const void* y, const void* bias, void* out, int64_t tokens, int n, int nh, int hd,
+                        int dtype, void* stream);
+
+/* Message describing the last error returned on the calling thread ("" if none). */
+SAMRS_API const char* samrs_last_error(void);
+
+/* SAMRS_ABI_VERSION of the loaded library. */
+SAMRS_API int samrs_abi_version(void);
+
+/*
+ * Device status word. Kernels never trap: a bounded wait that runs out, or an index check that
+ * fails, records a code here and the kernel returns early. samrs_device_status synchronises
+ * `stream`, returns the word of the current device (0 = healthy) and clears it when `clear` != 0.
+ * Codes: 1 = mbarrier/TMA wait timed out, 2 = MMA wait timed out, 3 = bad launch geometry.
+ */
+SAMRS_API int samrs_device_status(void* stream, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SAMRS_B200_H */

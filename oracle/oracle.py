@@ -1,0 +1,98 @@
+"""ctypes front end of the CPU oracle (oracle/relpos_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline
+leg. The product package never imports this module. Every function takes and returns float32 numpy
+arrays in the reference's layouts (q [bh,n,hd], kt [bh,hd,n], v [bh,n,hd], table [(2h-1)+(2w-1),hd]).
+"""
+import ctypes
+import os
+
+import numpy as np
+
+from . import build_oracle
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = build_oracle.OUT
+        if not os.path.exists(path):
+            build_oracle.build()
+        l = ctypes.CDLL(path)
+        f = ctypes.POINTER(ctypes.c_float)
+        L, I, F = ctypes.c_long, ctypes.c_int, ctypes.c_float
+        for name in ("oracle_attention_relpos_f32", "oracle_attention_relpos_bf16"):
+            fn = getattr(l, name)
+            fn.argtypes = [f, f, f, f, f, L, I, I, I, F, I]
+            fn.restype = I
+        l.oracle_relpos_softmax_f32.argtypes = [f, f, f, f, L, I, I, I, F, I]
+        l.oracle_relpos_softmax_f32.restype = I
+        l.oracle_qkv_split_f32.argtypes = [f, f, f, L, I, I, I]
+        l.oracle_qkv_split_f32.restype = I
+        l.oracle_cpu_has_bf16.restype = I
+        l.oracle_max_threads.restype = I
+        _lib = l
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def cpu_has_bf16() -> bool:
+    return bool(lib().oracle_cpu_has_bf16())
+
+
+def max_threads() -> int:
+    return int(lib().oracle_max_threads())
+
+
+def attention_relpos(q, kt, v, table, h, w, scale, threads=0, mode="exact"):
+    """Fused attention on the CPU. mode: "exact" (src/kernels.rs:131-225, f32) or "bf16"
+    (src/cpu_gemm.rs path, AVX-512 BF16 hosts only)."""
+    q, kt, v, table = _f32(q), _f32(kt), _f32(v), _f32(table)
+    bh, n, hd = q.shape
+    assert n == h * w and kt.shape == (bh, hd, n) and v.shape == (bh, n, hd)
+    assert table.shape == ((2 * h - 1) + (2 * w - 1), hd)
+    out = np.empty((bh, n, hd), np.float32)
+    fn = lib().oracle_attention_relpos_f32 if mode == "exact" else lib().oracle_attention_relpos_bf16
+    rc = fn(_p(q), _p(kt), _p(v), _p(table), _p(out), bh, h, w, hd, float(scale), int(threads))
+    if rc != 0:
+        raise RuntimeError(f"oracle attention ({mode}) failed: rc={rc}")
+    return out
+
+
+def relpos_softmax(s, q, table, h, w, scale, threads=0):
+    """Probabilities [rows, n] (src/kernels.rs:62-105). s: [..., n], q: [..., hd] with the same rows."""
+    n = h * w
+    s2, q2, table = _f32(s).reshape(-1, n), _f32(q), _f32(table)
+    hd = q2.shape[-1]
+    q2 = q2.reshape(-1, hd)
+    rows = s2.shape[0]
+    assert q2.shape[0] == rows
+    out = np.empty_like(s2)
+    rc = lib().oracle_relpos_softmax_f32(_p(s2), _p(q2), _p(table), _p(out), rows, h, w, hd, float(scale),
+                                         int(threads))
+    if rc != 0:
+        raise RuntimeError(f"oracle relpos_softmax failed: rc={rc}")
+    return out.reshape(np.shape(s))
+
+
+def qkv_split(y, bias, n, nh, hd):
+    """(q [bh,n,hd], kt [bh,hd,n], v [bh,n,hd]) from y [tokens, 3*nh*hd] + bias (src/kernels.rs:234-263)."""
+    y, bias = _f32(y), _f32(bias)
+    tokens = y.shape[0]
+    out = np.empty(3 * tokens * nh * hd, np.float32)
+    rc = lib().oracle_qkv_split_f32(_p(y), _p(bias), _p(out), tokens, n, nh, hd)
+    if rc != 0:
+        raise RuntimeError("oracle qkv_split failed")
+    bh = tokens // n * nh
+    plane = tokens * nh * hd
+    return (out[:plane].reshape(bh, n, hd), out[plane:2 * plane].reshape(bh, hd, n),
+            out[2 * plane:].reshape(bh, n, hd))

@@ -1,0 +1,183 @@
+"""sam-rs_b200: B200 (sm_100a) implementation of sam-rs's decomposed-rel-pos attention path.
+
+Host-side mirror of the reference's custom-op entry points (apiplant/sam-rs 0.1.1, src/kernels.rs),
+over the C ABI of libsamrs_b200.so. Same names, argument meaning and error behaviour as the
+reference; PyTorch CUDA tensors stand in for candle CUDA tensors (device memory and streams only).
+
+    relpos_softmax(scores, q, table, h, w, scale)        src/kernels.rs:12-43
+    attention_relpos(q, kt, v, table, h, w, scale)       src/kernels.rs:896-906 (the fused op, CUDA)
+    qkv_split(y, bias, n, nh, hd) -> (q, kt, v)          src/kernels.rs:870-894
+    bmm(a, b)                                            src/kernels.rs:917-924
+    Attention / window_partition / window_unpartition    src/sam1/encoder.rs:45-85, 132-145
+
+Every op runs a CUDA kernel of this package; a tensor that is not a contiguous CUDA tensor of
+f32/f16/bf16 raises, as the reference's `bail!` does (src/kernels.rs:1092,1097-1102). There is no
+CPU fallback: if libsamrs_b200.so is missing, the first op call raises.
+"""
+import math
+
+import torch
+
+from . import _abi
+from ._abi import SamrsError
+
+__all__ = ["relpos_softmax", "attention_relpos", "attention_relpos_cpu", "qkv_split", "bmm", "Attention",
+           "window_partition", "window_unpartition", "device_status", "SamrsError"]
+
+_DTYPES = {torch.float32: _abi.F32, torch.float16: _abi.F16, torch.bfloat16: _abi.BF16}
+_IMPLS = {"auto": _abi.IMPL_AUTO, "simt": _abi.IMPL_SIMT, "tc": _abi.IMPL_TC}
+
+
+def _dtype_code(*ts):
+    dt = ts[0].dtype
+    if dt not in _DTYPES:
+        raise SamrsError(_abi.ERR_INVALID, f"unsupported dtype {dt} for a sam-rs CUDA kernel")
+    for t in ts:
+        if t.dtype != dt:
+            raise SamrsError(_abi.ERR_INVALID, f"mixed dtypes {dt} and {t.dtype}")
+        if not t.is_cuda:
+            raise SamrsError(_abi.ERR_INVALID, "sam-rs CUDA kernels need CUDA tensors")
+        if not t.is_contiguous():
+            raise SamrsError(_abi.ERR_INVALID, "sam-rs kernels need contiguous inputs")
+    return _DTYPES[dt]
+
+
+def _stream():
+    return ctypes_stream(torch.cuda.current_stream())
+
+
+def ctypes_stream(stream):
+    return stream.cuda_stream
+
+
+def attention_relpos(q, kt, v, table, h, w, scale, impl="auto", out=None):
+    """Fused attention: softmax(scale*q.kt + relpos(q)) . v, shapes q/v [BH, h*w, hd], kt [BH, hd, h*w],
+    table [(2h-1)+(2w-1), hd]. Returns [BH, h*w, hd] in the input dtype (src/kernels.rs:896-906)."""
+    code = _dtype_code(q, kt, v, table)
+    if q.dim() != 3 or kt.dim() != 3 or v.dim() != 3:
+        raise SamrsError(_abi.ERR_INVALID, "attention_relpos: q, kt, v must be rank 3")
+    bh, n, hd = q.shape
+    if n != h * w or tuple(kt.shape) != (bh, hd, n) or tuple(v.shape) != (bh, n, hd):
+        raise SamrsError(_abi.ERR_INVALID, f"attention_relpos: shapes q{tuple(q.shape)} kt{tuple(kt.shape)} "
+                                           f"v{tuple(v.shape)} do not match h={h} w={w}")
+    if tuple(table.shape) != ((2 * h - 1) + (2 * w - 1), hd):
+        raise SamrsError(_abi.ERR_INVALID, f"attention_relpos: table {tuple(table.shape)} != "
+                                           f"({(2 * h - 1) + (2 * w - 1)}, {hd})")
+    if out is None:
+        out = torch.empty_like(q)
+    else:
+        _dtype_code(out, q)
+        if out.shape != q.shape:
+            raise SamrsError(_abi.ERR_INVALID, "attention_relpos: out shape mismatch")
+    _abi.check(_abi.lib().samrs_relpos_attn_fwd_ex(q.data_ptr(), kt.data_ptr(), v.data_ptr(), table.data_ptr(),
+                                                   out.data_ptr(), bh, h, w, hd, float(scale), code, _IMPLS[impl],
+                                                   _stream()))
+    return out
+
+
+def attention_relpos_cpu(q, kt, v, table, h, w, scale):
+    """Signature twin of the reference's `attention_relpos_cpu` (src/kernels.rs:899): returns the fused
+    attention for CUDA inputs, and None otherwise (the reference returns None off its own device)."""
+    if not (q.is_cuda and q.dtype in _DTYPES):
+        return None
+    return attention_relpos(q.contiguous(), kt.contiguous(), v.contiguous(), table.contiguous(), h, w, scale)
+
+
+def relpos_softmax(scores, q, table, h, w, scale):
+    """Materialising biased softmax: scores [BH, h*w, h*w], q [BH, h*w, hd] -> probs [BH, h*w, h*w]
+    (src/kernels.rs:12-43)."""
+    code = _dtype_code(scores, q, table)
+    n = h * w
+    hd = q.shape[-1]
+    rows = scores.numel() // n if n else 0
+    if scores.shape[-1] != n or q.numel() != rows * hd:
+        raise SamrsError(_abi.ERR_INVALID, f"relpos_softmax: scores {tuple(scores.shape)} / q {tuple(q.shape)} "
+                                           f"do not match h={h} w={w}")
+    if tuple(table.shape) != ((2 * h - 1) + (2 * w - 1), hd):
+        raise SamrsError(_abi.ERR_INVALID, "relpos_softmax: bad table shape")
+    out = torch.empty_like(scores)
+    _abi.check(_abi.lib().samrs_relpos_softmax_fwd(scores.data_ptr(), q.data_ptr(), table.data_ptr(),
+                                                   out.data_ptr(), rows, h, w, hd, float(scale), code, _stream()))
+    return out
+
+
+def qkv_split(y, bias, n, nh, hd):
+    """y [T, 3*nh*hd] (bias-free qkv projection) + bias [3*nh*hd] -> (q [BH,n,hd], kt [BH,hd,n], v [BH,n,hd]),
+    BH = (T/n)*nh (src/kernels.rs:870-894)."""
+    code = _dtype_code(y, bias)
+    t = y.shape[0]
+    if y.dim() != 2 or y.shape[1] != 3 * nh * hd or bias.numel() != 3 * nh * hd:
+        raise SamrsError(_abi.ERR_INVALID, "qkv_split: shape mismatch")
+    packed = torch.empty(y.numel(), dtype=y.dtype, device=y.device)
+    _abi.check(_abi.lib().samrs_qkv_split_fwd(y.data_ptr(), bias.data_ptr(), packed.data_ptr(), t, n, nh, hd, code,
+                                              _stream()))
+    bh = t // n * nh
+    plane = t * nh * hd
+    return (packed[:plane].view(bh, n, hd), packed[plane:2 * plane].view(bh, hd, n),
+            packed[2 * plane:].view(bh, n, hd))
+
+
+def bmm(a, b):
+    """Batched [B,m,k] x [B,k,n] (src/kernels.rs:917-924); a plain library GEMM, as in the reference."""
+    return torch.bmm(a, b)
+
+
+def device_status(clear=True):
+    """Synchronise the current stream and return the device status word (0 = healthy)."""
+    rc = _abi.lib().samrs_device_status(_stream(), 1 if clear else 0)
+    if rc < 0:
+        raise SamrsError(rc, _abi.lib().samrs_last_error().decode())
+    return rc
+
+
+def window_partition(x, ws):
+    """[B, H, W, C] -> ([B*nWh*nWw, ws, ws, C], Hp, Wp), zero-padding H, W up to multiples of ws
+    (src/sam1/encoder.rs:132-140)."""
+    b, h, w, c = x.shape
+    ph, pw = (ws - h % ws) % ws, (ws - w % ws) % ws
+    if ph or pw:
+        x = torch.nn.functional.pad(x, (0, 0, 0, pw, 0, ph))
+    hp, wp = h + ph, w + pw
+    x = x.reshape(b, hp // ws, ws, wp // ws, ws, c).permute(0, 1, 3, 2, 4, 5).contiguous()
+    return x.reshape(b * (hp // ws) * (wp // ws), ws, ws, c), hp, wp
+
+
+def window_unpartition(x, ws, hp, wp, hw, b, c):
+    """Inverse of window_partition, cropping back to hw (src/sam1/encoder.rs:142-145)."""
+    x = x.reshape(b, hp // ws, wp // ws, ws, ws, c).permute(0, 1, 3, 2, 4, 5).contiguous().reshape(b, hp, wp, c)
+    return x[:, : hw[0], : hw[1], :].contiguous()
+
+
+class Attention:
+    """SAM ViT attention block, `Attention::new` / `Attention::forward` of src/sam1/encoder.rs:45-85.
+
+    Weights: qkv_w [3C, C], qkv_b [3C], proj_w [C, C], rel_pos_h / rel_pos_w [2*input-1, hd].
+    The table is cat(rel_pos_h, rel_pos_w) and scale = hd^-0.5 (encoder.rs:56-69). forward() returns the
+    output projection without its bias, as the reference does (the caller fuses the bias into the
+    residual add, encoder.rs:71-72)."""
+
+    def __init__(self, qkv_w, qkv_b, proj_w, proj_b, rel_pos_h, rel_pos_w, heads):
+        dim = qkv_w.shape[1]
+        self.heads = heads
+        self.hd = dim // heads
+        self.qkv_wt = qkv_w.t().contiguous()
+        self.qkv_b = qkv_b.contiguous()
+        self.proj_wt = proj_w.t().contiguous()
+        self.proj_b = proj_b
+        self.scale = float(self.hd) ** -0.5
+        self.rel = torch.cat([rel_pos_h, rel_pos_w], 0).contiguous()
+
+    def forward(self, x):
+        nw, h, w, c = x.shape
+        nh, n = self.heads, h * w
+        hd = c // nh
+        y = (x.reshape(nw * n, c) @ self.qkv_wt).contiguous()
+        q, kt, v = qkv_split(y, self.qkv_b, n, nh, hd)
+        ctx = attention_relpos(q, kt, v, self.rel, h, w, self.scale)
+        out = ctx.reshape(nw, nh, n, hd).permute(0, 2, 1, 3).reshape(nw * n, c)
+        return (out @ self.proj_wt).reshape(nw, h, w, c)
+
+
+def vit_scale(hd):
+    """scale = hd^-0.5 (src/sam1/encoder.rs:66)."""
+    return 1.0 / math.sqrt(hd)

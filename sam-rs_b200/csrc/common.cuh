@@ -1,0 +1,39 @@
+// common.cuh - dtype helpers and the device status word shared by every kernel of the library.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace samrs {
+
+// Device status word (one per device, in the library's static device memory). Kernels never trap:
+// a bounded wait that runs out or a failed geometry check stores a nonzero code and the kernel
+// returns early; the host reads it with samrs_device_status().
+enum StatusCode : unsigned int {
+  kStatusOk = 0,
+  kStatusWaitTimeout = 1,  // mbarrier / TMA wait exceeded its iteration bound
+  kStatusMmaTimeout = 2,   // wait on a tcgen05 commit exceeded its bound
+  kStatusBadGeometry = 3,  // launch geometry does not match the kernel's assumptions
+};
+
+// The library is a single translation unit (samrs_abi.cu includes every kernel header), so the
+// word is defined here.
+__device__ unsigned int g_status = 0;
+
+__device__ __forceinline__ void report(unsigned int code) { atomicCAS(&g_status, 0u, code); }
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+}  // namespace samrs

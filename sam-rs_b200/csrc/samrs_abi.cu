@@ -1,0 +1,240 @@
+// samrs_abi.cu - the C ABI declared in include/samrs_b200.h: argument checks, dtype dispatch and
+// kernel selection. The entry points mirror the reference's candle ops (src/kernels.rs): they take
+// caller-owned device buffers, enqueue on the caller's stream, allocate nothing and never synchronise.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/samrs_b200.h"
+#include "common.cuh"
+#include "relpos_simt.cuh"
+#include "relpos_tc.cuh"
+
+namespace {
+
+using namespace samrs;
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_last_error[0] = '\0';
+  return SAMRS_OK;
+}
+
+int launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+size_t elem_size(int dtype) { return dtype == SAMRS_F32 ? 4 : 2; }
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Per-device cache of "is this an sm_100 device" and the opt-in shared memory limit.
+struct DevInfo {
+  int checked = 0;
+  int is_sm100 = 0;
+  int max_smem_optin = 0;
+  int num_sms = 0;
+};
+DevInfo g_dev[64];
+
+int device_info(DevInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(SAMRS_ERR_NODEVICE, "no CUDA device is current");
+  DevInfo& d = g_dev[dev];
+  if (!d.checked) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    d.is_sm100 = (major == 10 && minor == 0);
+    d.checked = 1;
+  }
+  if (!d.is_sm100) return fail(SAMRS_ERR_NODEVICE, "this library is built for sm_100a (B200) only");
+  *out = &d;
+  return SAMRS_OK;
+}
+
+int check_common(int64_t bh, int h, int w, int hd, int dtype, const char* what) {
+  if (dtype != SAMRS_F32 && dtype != SAMRS_F16 && dtype != SAMRS_BF16)
+    return fail(SAMRS_ERR_INVALID, "%s: unsupported dtype code %d (0 f32, 1 f16, 2 bf16)", what, dtype);
+  if (bh < 0) return fail(SAMRS_ERR_INVALID, "%s: negative batch-heads %lld", what, (long long)bh);
+  if (h < 1 || w < 1 || h > 128 || w > 128)
+    return fail(SAMRS_ERR_UNSUPPORTED, "%s: grid %dx%d outside 1..128", what, h, w);
+  if (hd < 1 || hd > kSimtMaxHd) return fail(SAMRS_ERR_UNSUPPORTED, "%s: head_dim %d outside 1..128", what, hd);
+  return SAMRS_OK;
+}
+
+template <typename T>
+int launch_simt(const void* q, const void* kt, const void* v, const void* table, void* out, int64_t bh, int h,
+                int w, int hd, float scale, cudaStream_t st, const DevInfo& dev) {
+  const int n = h * w;
+  const int64_t qtiles = (n + kSimtBQ - 1) / kSimtBQ;
+  const int64_t blocks = bh * qtiles;
+  if (blocks > 0x7fffffffLL) return fail(SAMRS_ERR_UNSUPPORTED, "relpos_attn: %lld CTAs exceed the grid limit", (long long)blocks);
+  const size_t smem = simt_smem_floats(h, w, hd) * sizeof(float);
+  if ((int)smem > dev.max_smem_optin)
+    return fail(SAMRS_ERR_UNSUPPORTED, "relpos_attn: %zu B of shared memory needed, %d available", smem,
+                dev.max_smem_optin);
+  auto kern = relpos_attn_simt<T>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return fail(SAMRS_ERR_LAUNCH, "relpos_attn: cannot set shared memory size %zu", smem);
+  kern<<<(unsigned)blocks, kSimtThreads, smem, st>>>(static_cast<const T*>(q), static_cast<const T*>(kt),
+                                                     static_cast<const T*>(v), static_cast<const T*>(table),
+                                                     static_cast<T*>(out), h, w, hd, scale);
+  return launch_status("relpos_attn_simt");
+}
+
+template <typename T>
+int launch_softmax(const void* s, const void* q, const void* table, void* out, int64_t rows, int h, int w, int hd,
+                   float scale, cudaStream_t st) {
+  if (rows > 0x7fffffffLL) return fail(SAMRS_ERR_UNSUPPORTED, "relpos_softmax: too many rows");
+  const size_t smem = (size_t)(hd + h + w) * sizeof(float);
+  relpos_softmax_rows<T><<<(unsigned)rows, kSoftmaxThreads, smem, st>>>(
+      static_cast<const T*>(s), static_cast<const T*>(q), static_cast<const T*>(table), static_cast<T*>(out), h, w, hd,
+      scale);
+  return launch_status("relpos_softmax_rows");
+}
+
+template <typename T>
+int launch_split(const void* y, const void* bias, void* out, int64_t tokens, int n, int nh, int hd, cudaStream_t st) {
+  const int64_t windows = tokens / n;
+  const int64_t gx = windows * nh;
+  const int gy = (n + kSplitTok - 1) / kSplitTok;
+  if (gx > 0x7fffffffLL || gy > 65535) return fail(SAMRS_ERR_UNSUPPORTED, "qkv_split: grid too large");
+  const size_t smem = (size_t)kSplitTok * (hd + 1) * sizeof(float);
+  qkv_split_kernel<T><<<dim3((unsigned)gx, gy), 256, smem, st>>>(static_cast<const T*>(y),
+                                                                 static_cast<const T*>(bias), static_cast<T*>(out),
+                                                                 tokens, n, nh, hd);
+  return launch_status("qkv_split");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* samrs_last_error(void) { return g_last_error; }
+
+int samrs_abi_version(void) { return SAMRS_ABI_VERSION; }
+
+int samrs_relpos_attn_fwd_ex(const void* q, const void* kt, const void* v, const void* table, void* out, int64_t bh,
+                             int h, int w, int hd, float scale, int dtype, int impl, void* stream) {
+  int rc = check_common(bh, h, w, hd, dtype, "relpos_attn");
+  if (rc) return rc;
+  if (impl != SAMRS_IMPL_AUTO && impl != SAMRS_IMPL_SIMT && impl != SAMRS_IMPL_TC)
+    return fail(SAMRS_ERR_INVALID, "relpos_attn: unknown impl %d", impl);
+  if (bh == 0) return ok();
+  if (!q || !kt || !v || !table || !out) return fail(SAMRS_ERR_INVALID, "relpos_attn: null pointer");
+  const size_t es = elem_size(dtype);
+  if (!aligned(q, es) || !aligned(kt, es) || !aligned(v, es) || !aligned(table, es) || !aligned(out, es))
+    return fail(SAMRS_ERR_INVALID, "relpos_attn: pointers must be aligned to the element size");
+  DevInfo* dev = nullptr;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  if (impl != SAMRS_IMPL_SIMT && dtype != SAMRS_F32) {
+    const TcShape shape = tc_select(h, w, hd, q, kt, v, out);
+    if (shape != TcShape::kNone) {
+      rc = dtype == SAMRS_BF16 ? tc_launch<__nv_bfloat16>(shape, q, kt, v, table, out, bh, h, w, hd, scale, st,
+                                                          dev->num_sms)
+                               : tc_launch<__half>(shape, q, kt, v, table, out, bh, h, w, hd, scale, st, dev->num_sms);
+      if (rc == 0) return launch_status("relpos_attn_tc");
+      return fail(SAMRS_ERR_LAUNCH, "relpos_attn_tc: %s", tc_error_string(rc));
+    }
+  }
+  if (impl == SAMRS_IMPL_TC)
+    return fail(SAMRS_ERR_UNSUPPORTED,
+                "relpos_attn: no tensor-core kernel for dtype %d, grid %dx%d, head_dim %d (or misaligned buffers)", dtype,
+                h, w, hd);
+  switch (dtype) {
+    case SAMRS_F32:
+      return launch_simt<float>(q, kt, v, table, out, bh, h, w, hd, scale, st, *dev);
+    case SAMRS_F16:
+      return launch_simt<__half>(q, kt, v, table, out, bh, h, w, hd, scale, st, *dev);
+    default:
+      return launch_simt<__nv_bfloat16>(q, kt, v, table, out, bh, h, w, hd, scale, st, *dev);
+  }
+}
+
+int samrs_relpos_attn_fwd(const void* q, const void* kt, const void* v, const void* table, void* out, int64_t bh,
+                          int h, int w, int hd, float scale, int dtype, void* stream) {
+  return samrs_relpos_attn_fwd_ex(q, kt, v, table, out, bh, h, w, hd, scale, dtype, SAMRS_IMPL_AUTO, stream);
+}
+
+int samrs_relpos_softmax_fwd(const void* s, const void* q, const void* table, void* out, int64_t rows, int h, int w,
+                             int hd, float scale, int dtype, void* stream) {
+  int rc = check_common(rows, h, w, hd, dtype, "relpos_softmax");
+  if (rc) return rc;
+  if ((int64_t)h * w > 16384) return fail(SAMRS_ERR_UNSUPPORTED, "relpos_softmax: row of %d exceeds 16384", h * w);
+  if (rows % ((int64_t)h * w) != 0)
+    return fail(SAMRS_ERR_INVALID, "relpos_softmax: rows (%lld) must be a multiple of h*w (%d)", (long long)rows, h * w);
+  if (rows == 0) return ok();
+  if (!s || !q || !table || !out) return fail(SAMRS_ERR_INVALID, "relpos_softmax: null pointer");
+  DevInfo* dev = nullptr;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SAMRS_F32:
+      return launch_softmax<float>(s, q, table, out, rows, h, w, hd, scale, st);
+    case SAMRS_F16:
+      return launch_softmax<__half>(s, q, table, out, rows, h, w, hd, scale, st);
+    default:
+      return launch_softmax<__nv_bfloat16>(s, q, table, out, rows, h, w, hd, scale, st);
+  }
+}
+
+int samrs_qkv_split_fwd(const void* y, const void* bias, void* out, int64_t tokens, int n, int nh, int hd, int dtype,
+                        void* stream) {
+  if (dtype != SAMRS_F32 && dtype != SAMRS_F16 && dtype != SAMRS_BF16)
+    return fail(SAMRS_ERR_INVALID, "qkv_split: unsupported dtype code %d", dtype);
+  if (tokens < 0 || n < 1 || nh < 1 || hd < 1 || hd > 1024)
+    return fail(SAMRS_ERR_INVALID, "qkv_split: bad geometry tokens=%lld n=%d nh=%d hd=%d", (long long)tokens, n, nh,
+                hd);
+  if (tokens % n != 0) return fail(SAMRS_ERR_INVALID, "qkv_split: tokens (%lld) not a multiple of n (%d)", (long long)tokens, n);
+  if (tokens == 0) return ok();
+  if (!y || !bias || !out) return fail(SAMRS_ERR_INVALID, "qkv_split: null pointer");
+  DevInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SAMRS_F32:
+      return launch_split<float>(y, bias, out, tokens, n, nh, hd, st);
+    case SAMRS_F16:
+      return launch_split<__half>(y, bias, out, tokens, n, nh, hd, st);
+    default:
+      return launch_split<__nv_bfloat16>(y, bias, out, tokens, n, nh, hd, st);
+  }
+}
+
+int samrs_device_status(void* stream, int clear) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "device_status: stream sync failed: %s", cudaGetErrorString(e));
+  unsigned int word = 0;
+  e = cudaMemcpyFromSymbol(&word, samrs::g_status, sizeof(word));
+  if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "device_status: read failed: %s", cudaGetErrorString(e));
+  if (clear && word) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(samrs::g_status, &zero, sizeof(zero));
+    if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "device_status: clear failed: %s", cudaGetErrorString(e));
+  }
+  return (int)word;
+}
+
+}  // extern "C"

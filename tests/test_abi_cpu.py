@@ -1,0 +1,74 @@
+"""The C-ABI library loads, exports every symbol that include/samrs_b200.h declares, and rejects bad
+arguments before touching a device (no compute call runs here)."""
+import ctypes
+
+import pytest
+
+from tests.conftest import load_samrs
+
+
+def abi():
+    return load_samrs()._abi
+
+
+def test_library_exports_every_header_symbol():
+    a = abi()
+    names = a.header_symbols()
+    assert set(names) >= {"samrs_relpos_attn_fwd", "samrs_relpos_attn_fwd_ex", "samrs_relpos_softmax_fwd",
+                          "samrs_qkv_split_fwd", "samrs_last_error", "samrs_abi_version", "samrs_device_status"}
+    lib = ctypes.CDLL(a.LIB_PATH)
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_abi_version():
+    assert abi().lib().samrs_abi_version() == 1
+
+
+@pytest.mark.parametrize("args,code", [
+    (dict(dtype=7), -1),                 # unknown dtype
+    (dict(bh=-1), -1),                   # negative batch
+    (dict(h=0), -2), (dict(w=129), -2),  # grid outside 1..128
+    (dict(hd=0), -2), (dict(hd=129), -2),
+    (dict(impl=9), -1),
+])
+def test_attention_rejects_bad_arguments(args, code):
+    a = abi()
+    p = dict(bh=1, h=4, w=4, hd=8, dtype=0, impl=0)
+    p.update(args)
+    rc = a.lib().samrs_relpos_attn_fwd_ex(0, 0, 0, 0, 0, p["bh"], p["h"], p["w"], p["hd"], 0.5, p["dtype"], p["impl"],
+                                          None)
+    assert rc == code
+    assert a.lib().samrs_last_error()
+
+
+def test_null_pointers_rejected():
+    a = abi()
+    assert a.lib().samrs_relpos_attn_fwd(0, 0, 0, 0, 0, 1, 4, 4, 8, 0.5, 0, None) == -1
+
+
+def test_empty_batch_is_noop():
+    a = abi()
+    assert a.lib().samrs_relpos_attn_fwd(0, 0, 0, 0, 0, 0, 4, 4, 8, 0.5, 2, None) == 0
+    assert a.lib().samrs_relpos_softmax_fwd(0, 0, 0, 0, 0, 4, 4, 8, 0.5, 1, None) == 0
+
+
+def test_softmax_rows_must_be_multiple_of_n():
+    a = abi()
+    assert a.lib().samrs_relpos_softmax_fwd(0, 0, 0, 0, 17, 4, 4, 8, 0.5, 0, None) == -1
+
+
+def test_qkv_split_rejects_ragged_tokens():
+    a = abi()
+    assert a.lib().samrs_qkv_split_fwd(0, 0, 0, 197, 196, 12, 64, 0, None) == -1
+
+
+def test_host_mirror_rejects_cpu_tensors():
+    import torch
+    s = load_samrs()
+    q = torch.zeros(1, 16, 8)
+    kt = torch.zeros(1, 8, 16)
+    t = torch.zeros(14, 8)
+    with pytest.raises(s.SamrsError):
+        s.attention_relpos(q, kt, q, t, 4, 4, 0.5)
+    assert s.attention_relpos_cpu(q, kt, q, t, 4, 4, 0.5) is None

@@ -1,0 +1,186 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle on the same seeded inputs.
+
+Bars (written here, not derived): f32 I/O max|got-ref|/max|ref| <= 1e-4; f16/bf16 I/O <= 3e-3 against
+the exact-f32 oracle fed the same 16-bit-rounded inputs (the reference's KAT rounds its inputs the same
+way, tests/kernels.rs:28-31). Geometries: the reference's KATs (tests/kernels.rs:23), config 1 at full
+size, ViT-L/H shapes, ragged and edge shapes; full-size ViT-H batches through size-independent
+properties (linearity in v, convex-combination bounds) plus oracle checks of sampled heads.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from tests.golden.make_golden import digest, f16_round, make_inputs as golden_inputs
+from tests.helpers import F32_TOL, HALF_TOL, make_inputs, rel_max_err
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "golden_*.npz")))
+
+
+def to_dev(a, dt, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev).to(DT[dt])
+
+
+def rounded(t):
+    return t.float().cpu().numpy()
+
+
+def run_case(samrs, dev, h, w, bh, hd, dt, impl, seed, scale=0.125, table_std=1.0):
+    q, kt, v, t = make_inputs(h, w, bh, hd, seed, table_std)
+    qd, ktd, vd, td = (to_dev(x, dt, dev) for x in (q, kt, v, t))
+    out = samrs.attention_relpos(qd, ktd, vd, td, h, w, scale, impl=impl)
+    assert samrs.device_status() == 0
+    ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, w, scale)
+    return rel_max_err(out.float().cpu().numpy(), ref)
+
+
+def tol(dt):
+    return F32_TOL if dt == "f32" else HALF_TOL
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=os.path.basename)
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+def test_golden_fixtures(samrs, cuda, path, dt):
+    # Fixture inputs are f16-representable, so f32 and f16 runs see identical values.
+    g = np.load(path)
+    h, w, bh, hd, seed = (int(g[k]) for k in ("h", "w", "bh", "hd", "seed"))
+    q, kt, v, t = golden_inputs(h, w, bh, hd, seed)
+    assert digest(q, kt, v, t) == str(g["input_sha256"])
+    out = samrs.attention_relpos(*(to_dev(x, dt, cuda) for x in (q, kt, v, t)), h, w, float(g["scale"]))
+    got = out.float().cpu().numpy()[:, g["rows"], :]
+    assert rel_max_err(got, g["out_rows"]) < tol(dt)
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("impl", ["auto", "simt"])
+@pytest.mark.parametrize("h,w,bh,hd", [(14, 14, 6, 64), (64, 64, 2, 64), (7, 11, 3, 80)])
+def test_reference_kat_geometries(samrs, cuda, h, w, bh, hd, dt, impl):
+    err = run_case(samrs, cuda, h, w, bh, hd, dt, impl, seed=h * 100 + w + bh)
+    assert err < tol(dt), err
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("h,w,bh,hd", [(64, 64, 3, 80), (14, 14, 37, 80), (14, 14, 50, 64), (64, 64, 4, 64)])
+def test_vit_shapes_tensor_core_path(samrs, cuda, h, w, bh, hd, dt):
+    err = run_case(samrs, cuda, h, w, bh, hd, dt, "auto", seed=bh * 7 + hd, table_std=0.5)
+    assert err < HALF_TOL, err
+
+
+@pytest.mark.parametrize("h,w,bh,hd,dt", [(1, 1, 3, 8, "f32"), (2, 3, 5, 1, "f32"), (3, 17, 2, 33, "bf16"),
+                                          (5, 5, 1, 128, "f16"), (128, 1, 1, 16, "f32"), (9, 64, 2, 72, "bf16"),
+                                          (32, 32, 1, 96, "f32")])
+def test_ragged_and_edge_shapes(samrs, cuda, h, w, bh, hd, dt):
+    err = run_case(samrs, cuda, h, w, bh, hd, dt, "auto", seed=h + w + hd)
+    assert err < tol(dt), err
+
+
+def test_config1_full_size_f32(samrs, cuda):
+    # ViT-B op, f32, one image. Windowed: 25 windows x 12 heads, 196 tokens, hd 64;
+    # global: 12 heads x 4096 tokens; rel tables ~ N(0, 0.5); scale 64^-0.5.
+    for (h, w, bh) in [(14, 14, 300), (64, 64, 12)]:
+        err = run_case(samrs, cuda, h, w, bh, 64, "f32", "auto", seed=bh, scale=64 ** -0.5, table_std=0.5)
+        assert err < F32_TOL, (h, err)
+
+
+@pytest.mark.parametrize("h,w,bh,hd", [(64, 64, 512, 80), (14, 14, 12800, 80)])
+def test_vith_full_batch_properties(samrs, cuda, h, w, bh, hd):
+    """Config 4 (ViT-H, B=32) at full size: linearity in v, convex-combination bounds, sampled heads vs oracle."""
+    g = torch.Generator(device=cuda).manual_seed(1234 + h)
+    n = h * w
+    q = torch.randn(bh, n, hd, device=cuda, generator=g).bfloat16()
+    kt = torch.randn(bh, hd, n, device=cuda, generator=g).bfloat16()
+    v1 = torch.randn(bh, n, hd, device=cuda, generator=g).bfloat16()
+    v2 = torch.randn(bh, n, hd, device=cuda, generator=g).bfloat16()
+    t = (torch.randn(4 * h - 2, hd, device=cuda, generator=g) * 0.5).bfloat16()
+    scale = hd ** -0.5
+    o1 = samrs.attention_relpos(q, kt, v1, t, h, w, scale)
+    o2 = samrs.attention_relpos(q, kt, v2, t, h, w, scale)
+    o12 = samrs.attention_relpos(q, kt, (v1.float() + v2.float()).bfloat16(), t, h, w, scale)
+    assert samrs.device_status() == 0
+    # softmax weights do not depend on v: out(v1+v2) = out(v1) + out(v2) up to bf16 rounding of v1+v2 and outputs
+    lin = (o12.float() - o1.float() - o2.float()).abs().max().item() / o12.float().abs().max().item()
+    assert lin < 2e-2, lin
+    # each output row is a convex combination of the rows of v
+    vmax = v1.float().amax(dim=1, keepdim=True)
+    vmin = v1.float().amin(dim=1, keepdim=True)
+    slack = 1e-2 * vmax.abs().clamp(min=1)
+    assert bool(((o1.float() <= vmax + slack) & (o1.float() >= vmin - slack)).all())
+    for b in (0, bh // 2 + 1, bh - 1):
+        ref = oracle.attention_relpos(rounded(q[b:b + 1]), rounded(kt[b:b + 1]), rounded(v1[b:b + 1]), rounded(t),
+                                      h, w, scale)
+        err = rel_max_err(o1[b:b + 1].float().cpu().numpy(), ref)
+        assert err < HALF_TOL, (b, err)
+
+
+def test_tc_and_simt_agree_bf16(samrs, cuda):
+    for (h, w, bh, hd) in [(64, 64, 2, 80), (14, 14, 40, 80)]:
+        q, kt, v, t = make_inputs(h, w, bh, hd, seed=99)
+        args = [to_dev(x, "bf16", cuda) for x in (q, kt, v, t)]
+        a = samrs.attention_relpos(*args, h, w, 0.125, impl="auto").float()
+        b = samrs.attention_relpos(*args, h, w, 0.125, impl="simt").float()
+        assert (a - b).abs().max().item() / b.abs().max().item() < HALF_TOL
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("h,w,bh,hd", [(14, 14, 6, 64), (64, 64, 2, 64), (7, 11, 3, 80)])
+def test_relpos_softmax_kat(samrs, cuda, h, w, bh, hd, dt):
+    # tests/kernels.rs:19-37: probs agree with the CPU op within 1e-3 absolute on 16-bit-rounded inputs
+    n = h * w
+    rng = np.random.default_rng(n + bh)
+    s = rng.standard_normal((bh, n, n), dtype=np.float32)
+    q = rng.standard_normal((bh, n, hd), dtype=np.float32)
+    t = rng.standard_normal((2 * h - 1 + 2 * w - 1, hd), dtype=np.float32)
+    sd, qd, td = (to_dev(x, dt, cuda) for x in (s, q, t))
+    got = samrs.relpos_softmax(sd, qd, td, h, w, 0.125).float().cpu().numpy()
+    want = oracle.relpos_softmax(rounded(sd), rounded(qd), rounded(td), h, w, 0.125)
+    bar = 1e-6 if dt == "f32" else 1e-3
+    assert np.abs(got - want).max() < bar
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+def test_qkv_split_matches_oracle(samrs, cuda, dt):
+    n, nh, hd, win = 196, 12, 64, 3
+    rng = np.random.default_rng(11)
+    y = rng.standard_normal((win * n, 3 * nh * hd), dtype=np.float32)
+    b = rng.standard_normal(3 * nh * hd, dtype=np.float32)
+    yd, bd = to_dev(y, dt, cuda), to_dev(b, dt, cuda)
+    got = samrs.qkv_split(yd, bd, n, nh, hd)
+    want = oracle.qkv_split(rounded(yd), rounded(bd), n, nh, hd)
+    for g_, w_ in zip(got, want):
+        ref = torch.from_numpy(w_).to(DT[dt]).float().numpy()  # the sum rounds once to the I/O dtype
+        assert np.array_equal(g_.float().cpu().numpy(), ref)
+
+
+def test_attention_block_chain(samrs, cuda):
+    """Attention::forward (src/sam1/encoder.rs:73-85) on a windowed ViT-B block: qkv GEMM -> qkv_split ->
+    fused attention -> proj, against the same chain with the oracle for the attention."""
+    torch.manual_seed(3)
+    c, nh = 768, 12
+    x = torch.randn(1, 64, 64, c, device=cuda)
+    parts, hp, wp = samrs.window_partition(x, 14)
+    assert parts.shape == (25, 14, 14, c) and hp == wp == 70
+    back = samrs.window_unpartition(parts, 14, hp, wp, (64, 64), 1, c)
+    assert torch.equal(back, x)
+    att = samrs.Attention(torch.randn(3 * c, c, device=cuda) * 0.02, torch.randn(3 * c, device=cuda) * 0.02,
+                          torch.randn(c, c, device=cuda) * 0.02, torch.zeros(c, device=cuda),
+                          torch.randn(27, 64, device=cuda) * 0.5, torch.randn(27, 64, device=cuda) * 0.5, nh)
+    y = att.forward(parts)
+    assert y.shape == parts.shape
+    qkv = (parts.reshape(-1, c) @ att.qkv_wt).cpu().numpy()
+    q, kt, v = oracle.qkv_split(qkv, att.qkv_b.cpu().numpy(), 196, nh, 64)
+    ctx = oracle.attention_relpos(q, kt, v, att.rel.cpu().numpy(), 14, 14, 64 ** -0.5)
+    ref = torch.from_numpy(ctx).reshape(25, nh, 196, 64).permute(0, 2, 1, 3).reshape(-1, c) @ att.proj_wt.cpu()
+    assert rel_max_err(y.reshape(-1, c).cpu().numpy(), ref.numpy()) < 1e-3
+
+
+def test_empty_and_status(samrs, cuda):
+    q = torch.zeros(0, 16, 8, device=cuda)
+    out = samrs.attention_relpos(q, torch.zeros(0, 8, 16, device=cuda), q, torch.zeros(14, 8, device=cuda), 4, 4, 1.0)
+    assert out.shape == (0, 16, 8)
+    assert samrs.device_status() == 0

@@ -1,0 +1,78 @@
+"""CPU oracle (oracle/relpos_oracle.c) against the golden fixtures and against the reference's own
+CPU-side tests (tests/cpu_gemm.rs:29-50 bf16-vs-exact bar, src/kernels.rs:887-893 qkv_split fallback)."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from tests.golden.make_golden import digest, f16_round, make_inputs
+from tests.helpers import make_inputs as make_rand, mean_rel_err, rel_max_err
+
+GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "golden_*.npz")))
+
+
+def load(path):
+    g = np.load(path)
+    h, w, bh, hd, seed = (int(g[k]) for k in ("h", "w", "bh", "hd", "seed"))
+    q, kt, v, t = make_inputs(h, w, bh, hd, seed)
+    assert digest(q, kt, v, t) == str(g["input_sha256"]), "fixture inputs no longer regenerate bit-identically"
+    return g, (h, w, bh, hd), (q, kt, v, t)
+
+
+def test_fixtures_present():
+    assert len(GOLDEN) == 4
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=os.path.basename)
+def test_exact_attention_matches_golden(path):
+    g, (h, w, bh, hd), (q, kt, v, t) = load(path)
+    out = oracle.attention_relpos(q, kt, v, t, h, w, float(g["scale"]))
+    assert rel_max_err(out[:, g["rows"], :], g["out_rows"]) < 1e-5
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=os.path.basename)
+def test_softmax_matches_golden(path):
+    g, (h, w, bh, hd), (q, kt, v, t) = load(path)
+    s = f16_round(np.matmul(q, kt))
+    p = oracle.relpos_softmax(s, q, t, h, w, float(g["scale"]))
+    assert np.abs(p[:, g["probs_row_ids"], :] - g["probs_rows"]).max() < 1e-5
+    np.testing.assert_allclose(p.sum(-1), 1.0, rtol=1e-5)
+
+
+@pytest.mark.skipif(not oracle.cpu_has_bf16(), reason="CPU lacks AVX-512 BF16")
+@pytest.mark.parametrize("h,w,bh,hd", [(14, 14, 6, 64), (64, 64, 2, 64), (7, 11, 3, 80)])
+def test_bf16_path_within_reference_bar(h, w, bh, hd):
+    # tests/cpu_gemm.rs:29-50: N(0,1) inputs, scale 0.125, mean relative error < 1.5e-2
+    q, kt, v, t = make_rand(h, w, bh, hd, seed=h * 1000 + w)
+    exact = oracle.attention_relpos(q, kt, v, t, h, w, 0.125)
+    fast = oracle.attention_relpos(q, kt, v, t, h, w, 0.125, mode="bf16")
+    assert mean_rel_err(fast, exact) < 1.5e-2
+
+
+def test_qkv_split_matches_tensor_fallback():
+    # src/kernels.rs:890-893: broadcast_add, reshape (t/n, n, 3, nh, hd), permute (2, 0, 3, 1, 4)
+    n, nh, hd, win = 196, 12, 64, 3
+    rng = np.random.default_rng(5)
+    y = rng.standard_normal((win * n, 3 * nh * hd), dtype=np.float32)
+    b = rng.standard_normal(3 * nh * hd, dtype=np.float32)
+    q, kt, v = oracle.qkv_split(y, b, n, nh, hd)
+    qkv = (y + b).reshape(win, n, 3, nh, hd).transpose(2, 0, 3, 1, 4).reshape(3, win * nh, n, hd)
+    np.testing.assert_array_equal(q, qkv[0])
+    np.testing.assert_array_equal(kt, qkv[1].transpose(0, 2, 1))
+    np.testing.assert_array_equal(v, qkv[2])
+
+
+@pytest.mark.parametrize("h,w,bh,hd", [(1, 1, 2, 8), (3, 5, 2, 16), (2, 9, 1, 7), (14, 14, 1, 80)])
+def test_ragged_shapes_match_float64(h, w, bh, hd):
+    from tests.golden.make_golden import reference_attention
+    q, kt, v, t = make_rand(h, w, bh, hd, seed=7 + h + w)
+    out = oracle.attention_relpos(q, kt, v, t, h, w, 0.3)
+    ref, _, _ = reference_attention(q, kt, v, t, h, w, 0.3)
+    assert rel_max_err(out, ref) < 1e-5
+
+
+def test_empty_batch():
+    q, kt, v, t = make_rand(4, 4, 0, 8, seed=1)
+    assert oracle.attention_relpos(q, kt, v, t, 4, 4, 0.5).shape == (0, 16, 8)
