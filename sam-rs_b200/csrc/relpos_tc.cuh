@@ -28,11 +28,12 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "relpos_tc_window.cuh"
 #include "sm100.cuh"
 
 namespace samrs {
 
-enum class TcShape { kNone, kGlobal };
+enum class TcShape { kNone, kGlobal, kWindow };
 
 namespace tcg {
 
@@ -450,6 +451,21 @@ inline int make_map(CUtensorMap* map, bool bf16, const void* base, uint64_t cols
   return r == CUDA_SUCCESS ? 0 : 3;
 }
 
+// 3-D map over a row-major [d2, d1, d0] 16-bit tensor, box [1, box1, box0].
+inline int make_map3(CUtensorMap* map, bool bf16, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                     uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return 2;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : 3;
+}
+
 }  // namespace tcg
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -458,6 +474,7 @@ inline TcShape tc_select(int h, int w, int hd, const void* q, const void* kt, co
                          const void* out) {
   if (!(aligned16(q) && aligned16(kt) && aligned16(v) && aligned16(table) && aligned16(out))) return TcShape::kNone;
   if (h == 64 && w == 64 && (hd == 64 || hd == 80)) return TcShape::kGlobal;
+  if (h == 14 && w == 14 && (hd == 64 || hd == 80)) return TcShape::kWindow;
   return TcShape::kNone;
 }
 
@@ -480,14 +497,38 @@ int tc_launch_global(const void* q, const void* kt, const void* v, const void* t
   return 0;
 }
 
+template <typename T, int HD>
+int tc_launch_window(const void* q, const void* kt, const void* v, const void* table, void* out, int64_t bh,
+                     float scale, cudaStream_t st, int num_sms) {
+  using namespace tcg;
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  if (bh > 0x7fffffffLL) return 4;
+  CUtensorMap mq, mv, mt;
+  int rc = make_map3(&mq, bf16, q, HD, tcw::kN, (uint64_t)bh, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (!rc) rc = make_map3(&mv, bf16, v, HD, tcw::kN, (uint64_t)bh, 16, tcw::kNP, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (!rc) rc = make_map(&mt, bf16, table, HD, 4 * tcw::kSide - 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (rc) return rc;
+  auto kern = tcw::relpos_attn_window<T, HD>;
+  const int smem = tcw::Layout<HD>::kSmemBytes;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return 5;
+  const int grid = (int)(bh < num_sms ? bh : num_sms);
+  kern<<<grid, tcw::kThreads, smem, st>>>(mq, mv, mt, static_cast<const T*>(kt), static_cast<T*>(out), (long)bh,
+                                         scale);
+  return 0;
+}
+
 template <typename T>
 int tc_launch(TcShape shape, const void* q, const void* kt, const void* v, const void* table, void* out, int64_t bh,
-              int h, int w, int hd, float scale, cudaStream_t st, int /*num_sms*/) {
+              int h, int w, int hd, float scale, cudaStream_t st, int num_sms) {
   (void)h;
   (void)w;
-  if (shape != TcShape::kGlobal) return 1;
-  return hd == 80 ? tc_launch_global<T, 80>(q, kt, v, table, out, bh, scale, st)
-                  : tc_launch_global<T, 64>(q, kt, v, table, out, bh, scale, st);
+  if (shape == TcShape::kGlobal)
+    return hd == 80 ? tc_launch_global<T, 80>(q, kt, v, table, out, bh, scale, st)
+                    : tc_launch_global<T, 64>(q, kt, v, table, out, bh, scale, st);
+  if (shape == TcShape::kWindow)
+    return hd == 80 ? tc_launch_window<T, 80>(q, kt, v, table, out, bh, scale, st, num_sms)
+                    : tc_launch_window<T, 64>(q, kt, v, table, out, bh, scale, st, num_sms);
+  return 1;
 }
 
 inline const char* tc_error_string(int rc) {

@@ -141,8 +141,11 @@ def test_relpos_softmax_kat(samrs, cuda, h, w, bh, hd, dt):
     sd, qd, td = (to_dev(x, dt, cuda) for x in (s, q, t))
     got = samrs.relpos_softmax(sd, qd, td, h, w, 0.125).float().cpu().numpy()
     want = oracle.relpos_softmax(rounded(sd), rounded(qd), rounded(td), h, w, 0.125)
-    bar = 1e-5 if dt == "f32" else 1e-3
-    assert np.abs(got - want).max() < bar
+    if dt == "bf16":
+        # bf16 rounding of a probability near 1 alone is 2^-9 ~ 2e-3: bound what lies beyond half an ulp
+        assert excess_err(got, want, "bf16") * np.abs(want).max() < 1e-3
+    else:
+        assert np.abs(got - want).max() < (1e-5 if dt == "f32" else 1e-3)
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
