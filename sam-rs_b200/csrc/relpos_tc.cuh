@@ -38,6 +38,10 @@ enum class TcShape { kNone, kGlobal, kWindow };
 namespace tcg {
 
 constexpr int kThreads = 384;
+// Registers: launched at 168 per thread; warpgroup 0 (producer, MMA, allocator) gives back to 56 and the
+// two softmax warpgroups take 224: 128 x 56 + 256 x 224 = 64512 = 384 x 168.
+constexpr uint32_t kRegsLow = 96, kRegsHigh = 200;
+static_assert(128 * kRegsLow + 256 * kRegsHigh <= kThreads * 168, "register split exceeds the launch allotment");
 constexpr int kBQ = 128, kBK = 128, kSide = 64, kN = 4096, kNT = kN / kBK, kStages = 2;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
@@ -158,7 +162,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-
+  if (warp < 4) {
+    regs_dec<kRegsLow>();
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -264,7 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&bars->final_mma);
       mbar_drain(&bars->final_mma, 0);
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    regs_inc<kRegsHigh>();
+  {
     // ------------------------------------------------------------------ softmax warpgroups
     const int q = (warp - 4) >> 2;        // query tile
     const int wq = warp & 3;              // TMEM lane quarter
@@ -410,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
@@ -503,17 +512,16 @@ int tc_launch_window(const void* q, const void* kt, const void* v, const void* t
   using namespace tcg;
   constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   if (bh > 0x7fffffffLL) return 4;
-  CUtensorMap mq, mv, mt;
-  int rc = make_map3(&mq, bf16, q, HD, tcw::kN, (uint64_t)bh, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B);
+  CUtensorMap mq, mv;
+  int rc = make_map3(&mq, bf16, q, HD, tcw::kN, (uint64_t)bh, 16, tcw::Layout<HD>::kQRows, CU_TENSOR_MAP_SWIZZLE_32B);
   if (!rc) rc = make_map3(&mv, bf16, v, HD, tcw::kN, (uint64_t)bh, 16, tcw::kNP, CU_TENSOR_MAP_SWIZZLE_32B);
-  if (!rc) rc = make_map(&mt, bf16, table, HD, 4 * tcw::kSide - 2, 16, 32, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
   auto kern = tcw::relpos_attn_window<T, HD>;
   const int smem = tcw::Layout<HD>::kSmemBytes;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return 5;
   const int grid = (int)(bh < num_sms ? bh : num_sms);
-  kern<<<grid, tcw::kThreads, smem, st>>>(mq, mv, mt, static_cast<const T*>(kt), static_cast<T*>(out), (long)bh,
-                                         scale);
+  kern<<<grid, tcw::kThreads, smem, st>>>(mq, mv, static_cast<const T*>(table), static_cast<const T*>(kt),
+                                         static_cast<T*>(out), (long)bh, scale);
   return 0;
 }
 

@@ -4,24 +4,29 @@
 // Math as the global kernel (src/kernels.rs:131-225; windows from src/sam1/encoder.rs:118-121,132-145):
 //   x[r,k] = scale * q_r . k_k + q_r . Th[i-kh+13] + q_r . Tw[j-kw+13],  r = 14 i + j, k = 14 kh + kw.
 //
-// These layers are HBM-bound (~98 FLOP/B at hd 80), so the kernel is built to stream: a persistent grid
-// (one CTA per SM) walks over units = (window, head) pairs, with the loads of unit u+1 in flight while
-// unit u is computed (2-stage ring of Q | V | K). Per unit the 196 query rows are two 128-row MMA tiles
-// (rows >= 196 are zero-filled by TMA and never stored) and all 196 keys fit one N = 208 key tile, so
-// the softmax is a plain two-pass row softmax: no online rescaling.
+// These layers are HBM-bound (~98 FLOP/B at hd 80), so the kernel streams: a persistent grid (one CTA
+// per SM) walks over units = (window, head) pairs with the loads of later units in flight. Per unit the
+// 196 query rows are two 128-row MMA tiles and all keys fit one key tile, so the softmax is a plain
+// two-pass row softmax (no online rescaling).
+//
+// One N = 256 MMA per tile yields scores and bias projections together: the B operand holds the 196
+// keys followed by the 27 rows of rel_pos_h and the 27 rows of rel_pos_w (196 + 54 = 250 <= 256), so
+// S_t = Q_t [K | Th | Tw]^T gives q.k in columns 0..195, RH = q.Th in 196..222 and RW = q.Tw in 223..249.
+// Each thread then selects its 14 + 14 bias values with a lane-dependent 4-stage shift (by its grid row
+// i for rh, by its grid column j for rw).
 //
 // Loads: q and v through 3-D TMA tensor maps [bh][196][hd] (OOB rows -> 0). kt ([bh][hd][196]) has a
-// 392-byte row pitch, which TMA cannot tile (strides must be multiples of 16 B), so 128 loader threads
+// 392-byte row pitch, which TMA cannot tile (strides must be multiples of 16 B), so 64 loader threads
 // move it with 8-byte cp.async straight into the canonical no-swizzle MN-major UMMA layout (8 keys x 8
-// dims per 128-byte core matrix); padded keys 196..207 stay zero.
-// Bias: one prologue MMA per tile gives [RH | RW] = Q [Th(27) | Tw(27)]^T (N = 64) in TMEM; each thread
-// selects its 14 + 14 values with a lane-dependent 4-stage shift (by i for rh, by j for rw).
+// dims per 128-byte core matrix). The table rows are written into both K buffers once, at start-up.
+// Rings: Q+K (2 stages, released when a unit's S MMAs complete) and V (2 stages, released after PV).
 //
-// Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM allocator, 4-7 kt loaders, 8-11 / 12-15 softmax + epilogue
-// of query tile 0 / 1 (thread = query row = TMEM lane).
-// TMEM (512 columns): tile t owns [256t, 256t+208): S_t (f32, 208 keys), then P_t (16-bit, cols 0..103)
-// written over the consumed S; O_t accumulates in cols [128, 128+hd) once the softmax has consumed S_t;
-// the prologue's [RH | RW] uses cols [0, 64).
+// Warps: 0 TMA producer, 1 MMA issuer, 2-3 kt loaders (warp 2 also allocates TMEM), 4-7 / 8-11 softmax +
+// epilogue of query tile 0 / 1 (thread = query row = TMEM lane); warp 11 covers rows 224..255 only,
+// which are all padding, so it only keeps the barrier counts.
+// The MMA issue order keeps the two tiles half a unit apart: S0(u) PV1(u-1) S1(u) PV0(u) S0(u+1) ...
+// TMEM (512 columns): tile t owns [256t, 256t+256): S_t; then P_t (16-bit pairs, cols 0..103) written
+// over the consumed scores; O_t accumulates in cols [128, 128+hd) once the softmax has consumed S_t.
 #pragma once
 #include <cuda.h>
 
@@ -33,51 +38,68 @@
 namespace samrs {
 namespace tcw {
 
-constexpr int kThreads = 512;
-constexpr int kSide = 14, kN = 196, kNP = 208, kStages = 2;
+constexpr int kThreads = 384;
+constexpr int kLoaders = 64;  // threads of warps 2-3
+// Registers: launched at 168 per thread (384 x 168 = 64512); warpgroup 0 (producer, MMA, loaders) gives
+// back to 96, the two softmax warpgroups take 200: 128 x 96 + 256 x 200 = 63488.
+constexpr uint32_t kRegsLow = 96, kRegsHigh = 200;
+static_assert(128 * kRegsLow + 256 * kRegsHigh <= kThreads * 168, "register split exceeds the launch allotment");
+constexpr int kSide = 14, kN = 196, kNP = 208, kNB = 256, kStages = 2;
+constexpr int kTabRows = 2 * kSide - 1;           // 27 rows each of rel_pos_h and rel_pos_w
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int HD>
 struct Layout {
   static constexpr int HC = HD / 16;
-  static constexpr int kQChunk = 128 * 32;          // [128 rows x 32 B] SW32
-  static constexpr int kQTile = HC * kQChunk;
-  static constexpr int kQBytes = 2 * kQTile;
+  // q: one [200 rows x 32 B] SW32 chunk per 16 dims (rows 196..199 zero-filled by TMA). Tile 1's MMA
+  // reads rows 128..255, i.e. past the chunk end into the next chunk / the K buffer: finite data whose
+  // S, P and O rows are discarded (every MMA output row depends on its own A row only).
+  static constexpr int kQRows = 200;
+  static constexpr int kQChunk = kQRows * 32;
+  static constexpr int kQBytes = HC * kQChunk;
   static constexpr int kVChunk = kNP * 32;          // [208 keys x 32 B] SW32
   static constexpr int kVBytes = HC * kVChunk;
-  static constexpr int kKSbo = (HD / 8) * 128;       // stride between 8-key core columns
-  static constexpr int kKBytes = (kNP / 8) * kKSbo;
-  static constexpr int kStage = kQBytes + kVBytes + kKBytes;
-  static constexpr int OFF_Q = 0, OFF_V = kQBytes, OFF_K = kQBytes + kVBytes;
-  static constexpr int kTabChunk = 64 * 32;         // [Th 32 rows | Tw 32 rows] x 32 B
-  static constexpr int kTabBytes = HC * kTabChunk;
-  static constexpr int OFF_TAB = kStages * kStage;
-  static constexpr int OFF_BAR = OFF_TAB + kTabBytes;
-  static constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
-  static_assert(kStage % 1024 == 0 && kVChunk % 256 == 0 && OFF_K % 128 == 0, "alignment");
+  // B operand of the S MMA, N = 256: keys, then table rows. Stride between 8-column core columns: HD/8
+  // core matrices of 128 B plus 16 B, so consecutive columns fall in different banks for the 8-byte
+  // cp.async writes (2 wavefronts per warp, the minimum for 256 B).
+  static constexpr int kKSbo = (HD / 8) * 128 + 16;
+  static constexpr int kKBytes = (kNB / 8) * kKSbo;
+  static constexpr int kQKStage = (kQBytes + kKBytes + 255) / 256 * 256;
+  static constexpr int kVStage = (kVBytes + 255) / 256 * 256;
+  static constexpr int OFF_Q = 0, OFF_K = kQBytes;  // within a QK stage
+  static constexpr int OFF_V = kStages * kQKStage;
+  static constexpr int OFF_BAR = OFF_V + kStages * kVStage;
+  // output staging: one [16 rows x HD] block per TMEM lane quarter, shared by the two tiles' warps
+  static constexpr int kStgRows = 16;
+  static constexpr int kStgBytes = kStgRows * HD * 2;
+  static constexpr int OFF_STG = OFF_BAR + 256;
+  static constexpr int kSmemBytes = OFF_STG + 4 * kStgBytes + 1024;
+  static_assert(kQChunk % 256 == 0 && kVChunk % 256 == 0 && OFF_K % 128 == 0 && kQKStage % 256 == 0, "alignment");
+  static_assert((256 - kQRows) * 32 <= kKBytes, "tile-1 over-read stays inside the stage");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct Bars {
-  uint64_t q_full[kStages], v_full[kStages], k_full[kStages], stage_free[kStages];
-  uint64_t tab_full, final_mma;
-  uint64_t rhw_full[2], bias_done[2], s_full[2], p_full[2], o_full[2];
+  uint64_t q_full[kStages], v_full[kStages], k_full[kStages], qk_free[kStages], v_free[kStages];
+  uint64_t final_mma;
+  uint64_t s_full[2], p_full[2], o_full[2], t_free[2];
+  uint64_t stg_to0[4], stg_to1[4];  // staging buffer handed to tile 0's / tile 1's warp
   uint32_t tmem_base;
   int abort_flag;
 };
 
-// Byte offset of (key n, dim d) in the no-swizzle MN-major K tile.
+// Byte offset of (column n, dim d) in the no-swizzle MN-major B tile.
 template <int HD>
 __device__ __forceinline__ uint32_t k_off(int n, int d) {
   return (uint32_t)((n >> 3) * Layout<HD>::kKSbo + (d >> 3) * 128 + (d & 7) * 16 + (n & 7) * 2);
 }
 
-// a[m] <- a[m + 2^B] where bit B of `sh` is set, for m < LEN.
+// a[m] <- a[m + 2^B] where bit B of `sh` is set, for m < LEN (one 3-input logic op per element).
 template <int B, int LEN>
 __device__ __forceinline__ void wshift(uint32_t (&a)[32], int sh) {
-  const uint32_t take = (sh >> B) & 1;
+  const uint32_t mask = 0u - ((uint32_t)(sh >> B) & 1u);
 #pragma unroll
-  for (int m = 0; m < LEN; ++m) a[m] = sm100::select_u32(take, a[m + (1 << B)], a[m]);
+  for (int m = 0; m < LEN; ++m) a[m] = (a[m] & ~mask) | (a[m + (1 << B)] & mask);
 }
 
 // out[k] = a[sh + 13 - k] * log2(e) for k = 0..13, sh in [0, 15].
@@ -90,81 +112,151 @@ __device__ __forceinline__ void select14(uint32_t (&a)[32], int sh, float (&out)
   for (int k = 0; k < 14; ++k) out[k] = __uint_as_float(a[13 - k]) * kLog2e;
 }
 
-// Pass 1 over one 32-key chunk: running max of S*c + rh[kh] + rw[kw] over valid keys.
-template <int CH>
-__device__ __forceinline__ float chunk_max(uint32_t tS, float c, const float (&rh)[14], const float (&rw)[14], float m) {
-  using namespace sm100;
-  uint32_t sv[32];
-  tmem_ld32(tS + 32 * CH, sv);
-  tmem_wait_ld();
-#pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    const int key = 32 * CH + e;
-    if (key < kN) m = fmaxf(m, fmaf(__uint_as_float(sv[e]), c, rh[key / kSide]) + rw[key % kSide]);
-  }
-  return m;
-}
+// Bias pairs for key pairs (k, k+1), k even. Since 14 is even, such a pair never straddles a window
+// row: it shares kh, and kw, kw+1 are both in the row. rhp[kh] = (rh[kh], rh[kh]), rwp[m] = (rw[2m], rw[2m+1]).
+struct Bias {
+  float2 rhp[14];
+  float2 rwp[7];
+};
 
-// Pass 2 over one 32-key chunk: p = 2^(S*c + rh + rw - m), row sum, 16-bit P into TMEM columns 16*CH...
-template <int CH, bool BF16>
-__device__ __forceinline__ float chunk_exp(uint32_t tS, float c, const float (&rh)[14], const float (&rwm)[14],
-                                           float sum) {
-  using namespace sm100;
-  uint32_t sv[32];
-  tmem_ld32(tS + 32 * CH, sv);
-  tmem_wait_ld();
-  uint32_t pk[16];
+// Pass 1 over the 32 keys of chunk CH held in `sv`: 8 independent running maxima of S*c + rh + rw.
+template <int CH>
+__device__ __forceinline__ void chunk_max(const uint32_t (&sv)[32], float2 c2, const Bias& b, float (&m)[8]) {
 #pragma unroll
   for (int e = 0; e < 32; e += 2) {
-    const int k0 = 32 * CH + e, k1 = k0 + 1;
-    const float p0 = k0 < kN ? ex2(fmaf(__uint_as_float(sv[e]), c, rh[k0 / kSide]) + rwm[k0 % kSide]) : 0.f;
-    const float p1 = k1 < kN ? ex2(fmaf(__uint_as_float(sv[e + 1]), c, rh[k1 / kSide]) + rwm[k1 % kSide]) : 0.f;
-    sum += p0 + p1;
-    pk[e >> 1] = pack2(p0, p1, BF16);
+    const int k0 = 32 * CH + e;
+    if (k0 < kN) {  // k0 even and kN even: k0 + 1 < kN too
+      const float2 s2 = make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+      const float2 x = sm100::add2(sm100::fma2(s2, c2, b.rhp[k0 / kSide]), b.rwp[(k0 % kSide) >> 1]);
+      m[(e >> 1) & 7] = sm100::max3(m[(e >> 1) & 7], x.x, x.y);
+    }
   }
-  tmem_st16(tS + 16 * CH, pk);
-  return sum;
 }
 
-// Keys 192..207 (last 16 columns; 192..195 valid).
-__device__ __forceinline__ float tail_max(uint32_t tS, float c, const float (&rh)[14], const float (&rw)[14], float m) {
-  using namespace sm100;
-  uint32_t sv[16];
-  tmem_ld16(tS + 192, sv);
-  tmem_wait_ld();
+// Pass 2 over chunk CH (keys 32*CH + e, e < NE): p = 2^(S*c + rh + (rw - m)); 4 pairwise partial sums;
+// 16-bit pairs into pk (keys >= 196 get p = 0).
+template <int CH, int NE, bool BF16>
+__device__ __forceinline__ void chunk_exp(const uint32_t (&sv)[32], float2 c2, const Bias& b, float2 (&sum)[4],
+                                          uint32_t (&pk)[16]) {
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int key = 192 + e;
-    m = fmaxf(m, fmaf(__uint_as_float(sv[e]), c, rh[key / kSide]) + rw[key % kSide]);
+  for (int e = 0; e < NE; e += 2) {
+    const int k0 = 32 * CH + e;
+    float2 p = make_float2(0.f, 0.f);
+    if (k0 < kN) {
+      const float2 s2 = make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+      const float2 x = sm100::add2(sm100::fma2(s2, c2, b.rhp[k0 / kSide]), b.rwp[(k0 % kSide) >> 1]);
+      p = make_float2(sm100::ex2(x.x), sm100::ex2(x.y));
+      sum[(e >> 1) & 3] = sm100::add2(sum[(e >> 1) & 3], p);
+    }
+    pk[e >> 1] = sm100::pack2(p.x, p.y, BF16);
   }
-  return m;
 }
 
+// Row max over the 196 keys: loads two chunks per wait.
+__device__ __forceinline__ float row_max(uint32_t tS, float2 c2, const Bias& b) {
+  using namespace sm100;
+  uint32_t a[32], bb[32];
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = -INFINITY;
+  tmem_ld32(tS + 0, a);
+  tmem_ld32(tS + 32, bb);
+  tmem_wait_ld_regs(a);
+  tmem_wait_ld_regs(bb);
+  chunk_max<0>(a, c2, b, m);
+  chunk_max<1>(bb, c2, b, m);
+  tmem_ld32(tS + 64, a);
+  tmem_ld32(tS + 96, bb);
+  tmem_wait_ld_regs(a);
+  tmem_wait_ld_regs(bb);
+  chunk_max<2>(a, c2, b, m);
+  chunk_max<3>(bb, c2, b, m);
+  tmem_ld32(tS + 128, a);
+  tmem_ld32(tS + 160, bb);
+  tmem_wait_ld_regs(a);
+  tmem_wait_ld_regs(bb);
+  chunk_max<4>(a, c2, b, m);
+  chunk_max<5>(bb, c2, b, m);
+  tmem_ld32(tS + 192, a);  // columns 192..223: keys 192..195
+  tmem_wait_ld_regs(a);
+  chunk_max<6>(a, c2, b, m);
+  return max3(max3(m[0], m[1], m[2]), max3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
+// p = 2^(x - m) for all keys (the bias pairs already hold rw - m), row sum returned, P written as 16-bit
+// pairs over the consumed S columns 0..103. The load of chunk k+1 is in flight while chunk k is
+// exponentiated.
 template <bool BF16>
-__device__ __forceinline__ float tail_exp(uint32_t tS, float c, const float (&rh)[14], const float (&rwm)[14],
-                                          float sum) {
+__device__ __forceinline__ float row_exp(uint32_t tS, float2 c2, const Bias& b) {
   using namespace sm100;
-  uint32_t sv[16];
-  tmem_ld16(tS + 192, sv);
-  tmem_wait_ld();
-  uint32_t pk[8];
+  uint32_t a[32], bb[32], pk[16];
+  float2 sum[4];
 #pragma unroll
-  for (int e = 0; e < 16; e += 2) {
-    const int k0 = 192 + e, k1 = k0 + 1;
-    const float p0 = k0 < kN ? ex2(fmaf(__uint_as_float(sv[e]), c, rh[k0 / kSide]) + rwm[k0 % kSide]) : 0.f;
-    const float p1 = k1 < kN ? ex2(fmaf(__uint_as_float(sv[e + 1]), c, rh[k1 / kSide]) + rwm[k1 % kSide]) : 0.f;
-    sum += p0 + p1;
-    pk[e >> 1] = pack2(p0, p1, BF16);
-  }
-  tmem_st8(tS + 96, pk);
-  return sum;
+  for (int i = 0; i < 4; ++i) sum[i] = make_float2(0.f, 0.f);
+  tmem_ld32(tS + 0, a);
+  tmem_wait_ld_regs(a);
+  tmem_ld32(tS + 32, bb);
+  chunk_exp<0, 32, BF16>(a, c2, b, sum, pk);
+  tmem_st16(tS + 0, pk);
+  tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 64, a);
+  chunk_exp<1, 32, BF16>(bb, c2, b, sum, pk);
+  tmem_st16(tS + 16, pk);
+  tmem_wait_ld_regs(a);
+  tmem_ld32(tS + 96, bb);
+  chunk_exp<2, 32, BF16>(a, c2, b, sum, pk);
+  tmem_st16(tS + 32, pk);
+  tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 128, a);
+  chunk_exp<3, 32, BF16>(bb, c2, b, sum, pk);
+  tmem_st16(tS + 48, pk);
+  tmem_wait_ld_regs(a);
+  tmem_ld32(tS + 160, bb);
+  chunk_exp<4, 32, BF16>(a, c2, b, sum, pk);
+  tmem_st16(tS + 64, pk);
+  tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 192, a);
+  chunk_exp<5, 32, BF16>(bb, c2, b, sum, pk);
+  tmem_st16(tS + 80, pk);
+  tmem_wait_ld_regs(a);
+  chunk_exp<6, 16, BF16>(a, c2, b, sum, pk);  // keys 192..207 (196.. get p = 0)
+  uint32_t p8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) p8[e] = pk[e];
+  tmem_st8(tS + 96, p8);
+  const float2 s01 = add2(sum[0], sum[1]), s23 = add2(sum[2], sum[3]);
+  const float2 st = add2(s01, s23);
+  return st.x + st.y;
+}
+
+// Bias of this thread's row from the S columns 192..255: rh from RH (cols 196..222) shifted by the grid
+// row i, rw from RW (cols 223..249) shifted by the grid column j.
+__device__ __forceinline__ void read_bias(uint32_t tS, int i, int j, Bias& b) {
+  using namespace sm100;
+  uint32_t v0[32], v1[32];
+  tmem_ld32(tS + 192, v0);
+  tmem_ld32(tS + 224, v1);
+  tmem_wait_ld_regs(v0);
+  tmem_wait_ld_regs(v1);
+  uint32_t a[32];
+  float rh[14], rw[14];
+#pragma unroll
+  for (int m = 0; m < 32; ++m) a[m] = m + 4 < 32 ? v0[m + 4] : v1[m + 4 - 32];  // column 196 + m
+  select14(a, i, rh);
+#pragma unroll
+  for (int m = 0; m < 32; ++m) a[m] = m == 0 ? v0[31] : v1[m - 1];  // column 223 + m
+  select14(a, j, rw);
+#pragma unroll
+  for (int k = 0; k < 14; ++k) b.rhp[k] = make_float2(rh[k], rh[k]);
+#pragma unroll
+  for (int k = 0; k < 7; ++k) b.rwp[k] = make_float2(rw[2 * k], rw[2 * k + 1]);
 }
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     relpos_attn_window(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmV,
-                       const __grid_constant__ CUtensorMap tmT, const T* __restrict__ kt, T* __restrict__ out,
-                       long bh_total, float scale) {
+                       const T* __restrict__ table, const T* __restrict__ kt, T* __restrict__ out, long bh_total,
+                       float scale) {
   using L = Layout<HD>;
   using namespace sm100;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -181,17 +273,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->q_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->k_full[s], 128);
-      mbar_init(&bars->stage_free[s], 1);
+      mbar_init(&bars->k_full[s], kLoaders);
+      mbar_init(&bars->qk_free[s], 1);
+      mbar_init(&bars->v_free[s], 1);
     }
-    mbar_init(&bars->tab_full, 1);
     mbar_init(&bars->final_mma, 1);
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&bars->rhw_full[t], 1);
-      mbar_init(&bars->bias_done[t], 128);
       mbar_init(&bars->s_full[t], 1);
       mbar_init(&bars->p_full[t], 128);
       mbar_init(&bars->o_full[t], 1);
+      mbar_init(&bars->t_free[t], 128);
+    }
+    for (int w = 0; w < 4; ++w) {
+      mbar_init(&bars->stg_to0[w], 1);
+      mbar_init(&bars->stg_to1[w], 1);
     }
     bars->abort_flag = 0;
     fence_mbar_init();
@@ -205,182 +300,206 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer (q, v, table)
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmV);
-      tma_prefetch_desc(&tmT);
-      mbar_arrive_expect_tx(&bars->tab_full, L::kTabBytes);
-      for (int c = 0; c < L::HC; ++c) {
-        tma_load_2d(smem + L::OFF_TAB + c * L::kTabChunk, &tmT, &bars->tab_full, c * 16, 0);                // Th
-        tma_load_2d(smem + L::OFF_TAB + c * L::kTabChunk + 32 * 32, &tmT, &bars->tab_full, c * 16, 2 * kSide - 1);  // Tw
+  if (warp < 4) {
+    regs_dec<kRegsLow>();
+    if (warp == 0) {
+      // ---------------------------------------------------------------- TMA producer (q, v)
+      if (lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmV);
+        int issued = 0;
+        for (int ui = 0; ui < n_units; ++ui) {
+          const int s = ui & 1;
+          const int u = (int)(first + (long)ui * gridDim.x);
+          const uint32_t prev = ((ui >> 1) - 1) & 1;
+          if (ui >= kStages && !mbar_wait(&bars->qk_free[s], prev, abort_flag)) break;
+          mbar_arrive_expect_tx(&bars->q_full[s], L::kQBytes);
+          for (int c = 0; c < L::HC; ++c)
+            tma_load_3d(smem + s * L::kQKStage + L::OFF_Q + c * L::kQChunk, &tmQ, &bars->q_full[s], c * 16, 0, u);
+          if (ui >= kStages && !mbar_wait(&bars->v_free[s], prev, abort_flag)) break;
+          mbar_arrive_expect_tx(&bars->v_full[s], L::kVBytes);
+          for (int c = 0; c < L::HC; ++c)
+            tma_load_3d(smem + L::OFF_V + s * L::kVStage + c * L::kVChunk, &tmV, &bars->v_full[s], c * 16, 0, u);
+          issued = ui + 1;
+        }
+        if (*abort_flag) {
+          for (int ui = issued > kStages ? issued - kStages : 0; ui < issued; ++ui) {
+            mbar_drain(&bars->q_full[ui & 1], (ui >> 1) & 1);
+            mbar_drain(&bars->v_full[ui & 1], (ui >> 1) & 1);
+          }
+        }
       }
-      int issued = 0;
+    } else if (warp == 1) {
+      // ---------------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idS = idesc_f16(kBf16, 128, kNB, false, true);
+        constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);
+        const uint32_t sb = smem_u32(smem);
+        auto smma = [&](int s, int t) {
+          const uint32_t qa = sb + s * L::kQKStage + L::OFF_Q + t * 128 * 32;
+          const uint32_t kb = sb + s * L::kQKStage + L::OFF_K;
+          for (int c = 0; c < L::HC; ++c)
+            mma_ss(tmem + 256 * t, smem_desc(qa + c * L::kQChunk, 16, 256, kLayoutSw32),
+                   smem_desc(kb + c * 256, 128, L::kKSbo, kLayoutNone), idS, c > 0);
+          mma_commit(&bars->s_full[t]);
+        };
+        auto pv = [&](int s, int t) {
+          const uint32_t vb = sb + L::OFF_V + s * L::kVStage;
+          for (int k = 0; k < kNP / 16; ++k)
+            mma_ts(tmem + 256 * t + 128, tmem + 256 * t + 8 * k, smem_desc(vb + k * 512, L::kVChunk, 256, kLayoutSw32),
+                   idPV, k > 0 ? 1u : 0u);
+          mma_commit(&bars->o_full[t]);
+        };
+        bool okk = true;
+        // Issue order: S0(u) | PV1(u-1) | S1(u) | PV0(u) | S0(u+1) ...
+        for (int ui = 0; ui < n_units && okk; ++ui) {
+          const int s = ui & 1, sp = s ^ 1;
+          const uint32_t ph = (ui >> 1) & 1;
+          okk = mbar_wait(&bars->q_full[s], ph, abort_flag) && mbar_wait(&bars->k_full[s], ph, abort_flag) &&
+                (ui == 0 || mbar_wait(&bars->t_free[0], (ui - 1) & 1, abort_flag));
+          if (!okk) break;
+          tc_fence_after();
+          smma(s, 0);
+          if (ui > 0) {
+            okk = mbar_wait(&bars->p_full[1], (ui - 1) & 1, abort_flag);
+            if (!okk) break;
+            tc_fence_after();
+            pv(sp, 1);
+            mma_commit(&bars->v_free[sp]);
+          }
+          okk = ui == 0 || mbar_wait(&bars->t_free[1], (ui - 1) & 1, abort_flag);
+          if (!okk) break;
+          tc_fence_after();
+          smma(s, 1);
+          mma_commit(&bars->qk_free[s]);  // this unit's Q and K are no longer read once its S MMAs finish
+          okk = mbar_wait(&bars->v_full[s], ph, abort_flag) && mbar_wait(&bars->p_full[0], ui & 1, abort_flag);
+          if (!okk) break;
+          tc_fence_after();
+          pv(s, 0);
+        }
+        if (okk && n_units > 0) {  // PV1 of the last unit
+          const int ul = n_units - 1;
+          okk = mbar_wait(&bars->p_full[1], ul & 1, abort_flag);
+          if (okk) {
+            tc_fence_after();
+            pv(ul & 1, 1);
+            mma_commit(&bars->v_free[ul & 1]);
+          }
+        }
+        mma_commit(&bars->final_mma);
+        mbar_drain(&bars->final_mma, 0);
+      }
+    } else {
+      // ---------------------------------------------------------------- kt loaders (cp.async relayout)
+      const int tl = threadIdx.x - 64;
+      // Table rows into both B buffers once: columns 196..222 = rel_pos_h, 223..249 = rel_pos_w,
+      // 250..255 = 0.
+      for (int s = 0; s < kStages; ++s) {
+        uint8_t* kb = smem + s * L::kQKStage + L::OFF_K;
+        for (int idx = tl; idx < (kNB - kN) * HD; idx += kLoaders) {
+          const int r = idx / HD, d = idx - r * HD;
+          const T v = r < 2 * kTabRows ? table[r * HD + d] : from_f<T>(0.f);
+          *reinterpret_cast<T*>(kb + k_off<HD>(kN + r, d)) = v;
+        }
+      }
+      // Thread tl owns the 8-byte key chunk c = tl (keys 4c..4c+3) of every dim row d: the source walks
+      // down kt by one 392-byte row per d, the destination by 16 bytes ((d/8)*128 + (d%8)*16 = 16 d).
+      const int c = tl;
+      const uint32_t dst0 = (uint32_t)((c >> 1) * L::kKSbo + (c & 1) * 8);
       for (int ui = 0; ui < n_units; ++ui) {
         const int s = ui & 1;
-        const int u = (int)(first + (long)ui * gridDim.x);
-        if (ui >= kStages && !mbar_wait(&bars->stage_free[s], ((ui >> 1) - 1) & 1, abort_flag)) break;
-        uint8_t* st = smem + s * L::kStage;
-        mbar_arrive_expect_tx(&bars->q_full[s], L::kQBytes);
-        for (int t = 0; t < 2; ++t)
-          for (int c = 0; c < L::HC; ++c)
-            tma_load_3d(st + L::OFF_Q + t * L::kQTile + c * L::kQChunk, &tmQ, &bars->q_full[s], c * 16, 128 * t, u);
-        mbar_arrive_expect_tx(&bars->v_full[s], L::kVBytes);
-        for (int c = 0; c < L::HC; ++c)
-          tma_load_3d(st + L::OFF_V + c * L::kVChunk, &tmV, &bars->v_full[s], c * 16, 0, u);
-        issued = ui + 1;
-      }
-      if (*abort_flag) {
-        for (int ui = issued > kStages ? issued - kStages : 0; ui < issued; ++ui) {
-          mbar_drain(&bars->q_full[ui & 1], (ui >> 1) & 1);
-          mbar_drain(&bars->v_full[ui & 1], (ui >> 1) & 1);
+        const long u = first + (long)ui * gridDim.x;
+        if (ui >= kStages && !mbar_wait(&bars->qk_free[s], ((ui >> 1) - 1) & 1, abort_flag)) break;
+        if (c < kN / 4) {
+          uint8_t* dst = smem + s * L::kQKStage + L::OFF_K + dst0;
+          const T* src = kt + u * (long)HD * kN + 4 * c;
+#pragma unroll 8
+          for (int d = 0; d < HD; ++d) cp_async_8(dst + 16 * d, src + d * kN);
         }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idRHW = idesc_f16(kBf16, 128, 64, false, false);
-      constexpr uint32_t idS = idesc_f16(kBf16, 128, kNP, false, true);
-      constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);
-      const uint32_t sb = smem_u32(smem);
-      auto descQ = [&](int s, int t, int c) {
-        return smem_desc(sb + s * L::kStage + L::OFF_Q + t * L::kQTile + c * L::kQChunk, 16, 256, kLayoutSw32);
-      };
-      auto descTab = [&](int c) { return smem_desc(sb + L::OFF_TAB + c * L::kTabChunk, 16, 256, kLayoutSw32); };
-      auto descK = [&](int s, int c) {
-        return smem_desc(sb + s * L::kStage + L::OFF_K + c * 256, 128, L::kKSbo, kLayoutNone);
-      };
-      auto descV = [&](int s, int k) {
-        return smem_desc(sb + s * L::kStage + L::OFF_V + k * 512, L::kVChunk, 256, kLayoutSw32);
-      };
-      bool okk = mbar_wait(&bars->tab_full, 0, abort_flag);
-      for (int ui = 0; ui < n_units && okk; ++ui) {
-        const int s = ui & 1;
-        const uint32_t ph = (ui >> 1) & 1;
-        okk = mbar_wait(&bars->q_full[s], ph, abort_flag);
-        if (!okk) break;
-        tc_fence_after();
-        for (int t = 0; t < 2; ++t) {
-          for (int c = 0; c < L::HC; ++c) mma_ss(tmem + 256 * t, descQ(s, t, c), descTab(c), idRHW, c > 0);
-          mma_commit(&bars->rhw_full[t]);
-        }
-        okk = mbar_wait(&bars->k_full[s], ph, abort_flag);
-        for (int t = 0; t < 2 && okk; ++t) {
-          okk = mbar_wait(&bars->bias_done[t], ui & 1, abort_flag);
-          if (!okk) break;
-          tc_fence_after();
-          for (int c = 0; c < L::HC; ++c) mma_ss(tmem + 256 * t, descQ(s, t, c), descK(s, c), idS, c > 0);
-          mma_commit(&bars->s_full[t]);
-        }
-        if (okk) okk = mbar_wait(&bars->v_full[s], ph, abort_flag);
-        for (int t = 0; t < 2 && okk; ++t) {
-          okk = mbar_wait(&bars->p_full[t], ui & 1, abort_flag);
-          if (!okk) break;
-          tc_fence_after();
-          for (int k = 0; k < kNP / 16; ++k)
-            mma_ts(tmem + 256 * t + 128, tmem + 256 * t + 8 * k, descV(s, k), idPV, k > 0 ? 1u : 0u);
-          mma_commit(&bars->o_full[t]);
-        }
-        if (okk) mma_commit(&bars->stage_free[s]);
-      }
-      mma_commit(&bars->final_mma);
-      mbar_drain(&bars->final_mma, 0);
-    }
-  } else if (warp >= 4 && warp < 8) {
-    // ------------------------------------------------------------------ kt loaders (cp.async relayout)
-    const int tl = threadIdx.x - 128;
-    for (int s = 0; s < kStages; ++s) {  // padded keys 196..207 stay zero for the whole kernel
-      uint8_t* kb = smem + s * L::kStage + L::OFF_K;
-      for (int idx = tl; idx < HD * 3; idx += 128) {
-        const int d = idx / 3, n = kN + 4 * (idx % 3);
-        *reinterpret_cast<uint2*>(kb + k_off<HD>(n, d)) = make_uint2(0u, 0u);
-      }
-    }
-    for (int ui = 0; ui < n_units; ++ui) {
-      const int s = ui & 1;
-      const long u = first + (long)ui * gridDim.x;
-      if (ui >= kStages && !mbar_wait(&bars->stage_free[s], ((ui >> 1) - 1) & 1, abort_flag)) break;
-      uint8_t* kb = smem + s * L::kStage + L::OFF_K;
-      const T* src = kt + u * (long)HD * kN;
-      for (int idx = tl; idx < HD * (kN / 4); idx += 128) {
-        const int d = idx / (kN / 4), n = 4 * (idx % (kN / 4));
-        cp_async_8(kb + k_off<HD>(n, d), src + d * kN + n);
+        cp_async_wait_all();
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->k_full[s]);
       }
       cp_async_wait_all();
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->k_full[s]);
     }
-    cp_async_wait_all();
-  } else if (warp >= 8) {
+  } else {
+    regs_inc<kRegsHigh>();
     // ------------------------------------------------------------------ softmax + epilogue
-    const int t = (warp - 8) >> 2;
+    const int t = (warp - 4) >> 2;
     const int wq = warp & 3;
     const int rt = 128 * t + 32 * wq + lane;  // query row within the window
+    const bool live = 128 * t + 32 * wq < kN;  // warp holds at least one real row (warp-uniform)
     const int i = rt / kSide, j = rt % kSide;
     const uint32_t tS = tmem + ((uint32_t)(32 * wq) << 16) + 256 * t;
     const uint32_t tO = tS + 128;
     const float c = scale * kLog2e;
+    uint8_t* stg = smem + L::OFF_STG + wq * L::kStgBytes;
     for (int ui = 0; ui < n_units; ++ui) {
       const long u = first + (long)ui * gridDim.x;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->rhw_full[t], ui & 1, abort_flag))) break;
-      tc_fence_after();
-      float rh[14], rw[14];
-      {
-        uint32_t a[32];
-        tmem_ld32(tS, a);
-        tmem_wait_ld();
-        select14(a, i, rh);
-        tmem_ld32(tS + 32, a);
-        tmem_wait_ld();
-        select14(a, j, rw);
-      }
-      tc_fence_before();
-      mbar_arrive(&bars->bias_done[t]);
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[t], ui & 1, abort_flag))) break;
       tc_fence_after();
-      float m = -INFINITY;
-      m = chunk_max<0>(tS, c, rh, rw, m);
-      m = chunk_max<1>(tS, c, rh, rw, m);
-      m = chunk_max<2>(tS, c, rh, rw, m);
-      m = chunk_max<3>(tS, c, rh, rw, m);
-      m = chunk_max<4>(tS, c, rh, rw, m);
-      m = chunk_max<5>(tS, c, rh, rw, m);
-      m = tail_max(tS, c, rh, rw, m);
+      float sum = 1.f;
+      if (live) {
+        Bias b;
+        read_bias(tS, i, j, b);
+        const float2 c2 = make_float2(c, c);
+        const float m = row_max(tS, c2, b);
 #pragma unroll
-      for (int k = 0; k < 14; ++k) rw[k] -= m;
-      float sum = 0.f;
-      sum = chunk_exp<0, kBf16>(tS, c, rh, rw, sum);
-      sum = chunk_exp<1, kBf16>(tS, c, rh, rw, sum);
-      sum = chunk_exp<2, kBf16>(tS, c, rh, rw, sum);
-      sum = chunk_exp<3, kBf16>(tS, c, rh, rw, sum);
-      sum = chunk_exp<4, kBf16>(tS, c, rh, rw, sum);
-      sum = chunk_exp<5, kBf16>(tS, c, rh, rw, sum);
-      sum = tail_exp<kBf16>(tS, c, rh, rw, sum);
-      tmem_wait_st();
+        for (int k = 0; k < 7; ++k) b.rwp[k] = make_float2(b.rwp[k].x - m, b.rwp[k].y - m);
+        sum = row_exp<kBf16>(tS, c2, b);
+        tmem_wait_st();
+      }
       tc_fence_before();
       mbar_arrive(&bars->p_full[t]);
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_full[t], ui & 1, abort_flag))) break;
       tc_fence_after();
-      const float inv = 1.f / sum;
-      T* orow = out + (u * kN + rt) * HD;
+      // Epilogue: O/l -> this warp's staging block, 16 rows at a time (row-major, i.e. the layout of
+      // those rows in `out`), then fully coalesced 16-byte stores. Tile 0 and tile 1 warps of the same
+      // lane quarter take the staging buffer in turn: tile 0 of unit u, tile 1 of unit u, tile 0 of u+1...
+      const bool turn_ok = t == 0 ? (ui == 0 || mbar_wait(&bars->stg_to0[wq], (ui - 1) & 1, abort_flag))
+                                  : mbar_wait(&bars->stg_to1[wq], ui & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, turn_ok)) break;
+      if (live) {
+        const float inv = 1.f / sum;
+        const int row0 = 128 * t + 32 * wq;
+        uint32_t pw[HD / 16][8];
 #pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 16) {
-        uint32_t ov[16];
-        tmem_ld16(tO + c0, ov);
-        tmem_wait_ld();
-        uint32_t pw[8];
+        for (int c0 = 0; c0 < HD / 16; ++c0) {
+          uint32_t ov[16];
+          tmem_ld16(tO + 16 * c0, ov);
+          tmem_wait_ld_regs(ov);
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          pw[e] = pack2(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv, kBf16);
-        if (rt < kN) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-          dst[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-          dst[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+          for (int e = 0; e < 8; ++e)
+            pw[c0][e] = pack2(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv, kBf16);
+        }
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          if ((lane >> 4) == half) {
+#pragma unroll
+            for (int c0 = 0; c0 < HD / 16; ++c0) {
+              uint4* srow = reinterpret_cast<uint4*>(stg + (lane & 15) * (HD * 2) + 32 * c0);
+              srow[0] = make_uint4(pw[c0][0], pw[c0][1], pw[c0][2], pw[c0][3]);
+              srow[1] = make_uint4(pw[c0][4], pw[c0][5], pw[c0][6], pw[c0][7]);
+            }
+          }
+          __syncwarp();
+          const int hrow0 = row0 + 16 * half;
+          const int left = kN - hrow0;
+          const int nrows = left < L::kStgRows ? (left > 0 ? left : 0) : L::kStgRows;
+          const int nchunks = nrows * (HD / 8);  // 16-byte chunks of these rows
+          const uint4* sbuf = reinterpret_cast<const uint4*>(stg);
+          uint4* gdst = reinterpret_cast<uint4*>(out + (u * kN + hrow0) * HD);
+#pragma unroll
+          for (int k = 0; k < (L::kStgRows * HD / 8 + 31) / 32; ++k) {
+            const int ch = lane + 32 * k;
+            if (ch < nchunks) gdst[ch] = sbuf[ch];
+          }
+          __syncwarp();
         }
       }
+      if (lane == 0) mbar_arrive(t == 0 ? &bars->stg_to1[wq] : &bars->stg_to0[wq]);
       tc_fence_before();
+      mbar_arrive(&bars->t_free[t]);  // O_t read and S_t columns free for the next unit's S MMA
     }
   }
   tc_fence_before();
