@@ -176,7 +176,8 @@ def cpu_sample(images=1, seed=7):
     import numpy as np
     from oracle import oracle
     mode = "bf16" if oracle.cpu_has_bf16() else "exact"
-    threads = oracle.max_threads()
+    # all host threads this process may use (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     rng = np.random.default_rng(seed)
     sets = {}
     for kind, h, w, bh in {g[:3] + (g[3],) for g in layer_geoms(images)}:
