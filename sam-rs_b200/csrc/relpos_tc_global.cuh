@@ -1,0 +1,581 @@
+// relpos_tc_global.cuh - tcgen05 (sm_100a tensor-core) kernel for SAM's global layers (64x64 tokens,
+// head_dim 64 or 80, f16/bf16 I/O, f32 accumulation and softmax).
+//
+// Math (src/kernels.rs:131-225 restated, src/sam1/encoder.rs:73-85):
+//   x[r,k] = scale * q_r . k_k + q_r . Th[i-kh+63] + q_r . Tw[j-kw+63],   out_r = sum_k softmax_k(x) v_k
+// with r = 64 i + j and k = 64 kh + kw.
+//
+// One CTA = one head (bh) x 256 query rows (two 128-row tiles Q0, Q1 = grid rows I0..I0+3), looping
+// over 32 key tiles of 128 keys (grid rows kh = 2t, 2t+1); both query tiles share every K/V tile.
+// 20 warps:
+//   warp 0       TMA producer: Q0, Q1 and the two table slices once, then K and V tiles (3-stage rings)
+//   warp 1       MMA issuer (one thread): prologue bias MMAs, then per tile and query tile, in order,
+//                O_q += P_q(t) V(t) and S_q(t+1) = Q_q K(t+1)^T. In-order issue lets S_q(t+1) overwrite
+//                P_q(t) (both live in the S_q columns) without a round trip through a barrier.
+//   warp 2       TMEM allocator (512 columns)
+//   warps 4-11   softmax of Q0, warps 12-19 softmax of Q1: two warps per TMEM lane quarter, one per
+//                16-lane half. With the 16x256b access shape four threads share a row pair (rows r and
+//                r+8 of the half), each holding key pairs 8m + 2(t%4), +1: 64 scores per thread and
+//                tile, row maxima and sums combined with two shuffles. Four softmax warps per SM
+//                sub-partition keep the exp unit busy while the other query tile waits on its MMAs.
+//
+// Rel-pos bias, computed in-tile: the prologue MMAs give RW = Q Tw^T (128 cols) and RH = Q Th[I0..I0+79]^T
+// (80 cols) in TMEM. rw: each warp reads RW for its lane quarter, a lane-dependent barrel shift selects
+// row r's window j..j+63 (reversed, = rw[kw]) and shuffles hand each thread the 16 values of its key
+// pairs for its two rows (log2 units, in registers). rh: parked in shared memory as [kh][row]; a key tile
+// needs two rh values per row (one per 64-key half).
+// The softmax is online in the log2 domain with conditional rescaling (O is rescaled only when the row
+// max grows by more than 8); P is written back as 16-bit pairs into the S columns of TMEM and fed to the
+// PV MMA as the A operand straight from TMEM. No score ever reaches HBM.
+//
+// TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O0 [256,256+HD), O1 [256+HD, 256+2HD); prologue:
+// RW_q in S_q, RH_q at [256+80q, 256+80q+80).
+// Shared memory (1 KB aligned): Q0 | Q1 | K ring | V ring | RH park (tables alias it in the prologue) | barriers.
+#pragma once
+#include <cuda.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace samrs {
+namespace tcg {
+
+constexpr int kThreads = 640;
+constexpr int kLaunchRegs = 96;  // 65536 / 640 rounded down to the allocation granularity
+// Registers: warpgroup 0 (producer, issuer, allocator) gives back to 64 and the four softmax warpgroups
+// take 104: 128 x 64 + 512 x 104 = 61440 = 640 x 96.
+constexpr uint32_t kRegsLow = 64, kRegsHigh = 104;
+static_assert(128 * kRegsLow + 512 * kRegsHigh <= kThreads * kLaunchRegs, "register split exceeds the launch allotment");
+constexpr int kBQ = 128, kBK = 128, kSide = 64, kN = 4096, kNT = kN / kBK, kStages = 3;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.f;  // log2 units
+
+template <int HD>
+struct Layout {
+  static constexpr int HC = HD / 16;                  // 16-element (32 B) chunks of a row
+  static constexpr int kChunkBytes = 128 * 32;        // one [128 rows x 32 B] SW32 chunk
+  static constexpr int kQBytes = HC * kChunkBytes;    // a 128-row tile of q / v / table
+  static constexpr int kKAtom = HD * 128;             // one [HD rows x 64 keys] SW128 box
+  static constexpr int kKBytes = 2 * kKAtom;
+  static constexpr int kVBytes = kQBytes;
+  static constexpr int kRhBytes = 64 * 256 * 4;       // rh park: [kh][256 rows] f32
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + 2 * kQBytes;
+  static constexpr int OFF_V = OFF_K + kStages * kKBytes;
+  static constexpr int OFF_RH = OFF_V + kStages * kVBytes;
+  static constexpr int OFF_TH = OFF_RH;               // prologue only (aliases the rh park)
+  static constexpr int OFF_TW = OFF_RH + kQBytes;
+  static constexpr int OFF_BAR = OFF_RH + kRhBytes;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = OFF_BAR + kBarBytes + 1024;  // + alignment slack
+  static_assert(2 * kQBytes <= kRhBytes, "tables must fit in the rh park");
+  static_assert(kKAtom % 1024 == 0 && OFF_K % 1024 == 0 && OFF_V % 1024 == 0, "SW128 atoms need 1 KB alignment");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+struct Bars {
+  uint64_t q_full, pro_done, final_mma;
+  uint64_t k_full[kStages], v_full[kStages], k_empty[kStages], v_empty[kStages];
+  uint64_t bias_done[2], s_full[2], p_full[2], o_done[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+
+// One stage of the lane-dependent shift: a[m] <- a[m + 2^B] where bit B of the lane is set.
+template <int B, int LEN>
+__device__ __forceinline__ void shift_stage(uint32_t (&a)[48], int lane) {
+  const uint32_t mask = 0u - ((uint32_t)(lane >> B) & 1u);
+#pragma unroll
+  for (int m = 0; m < LEN; ++m) a[m] = (a[m] & ~mask) | (a[m + (1 << B)] & mask);
+}
+
+// rw block C of the row on this lane (32x32b access): blk[i] = rw[16C + i] (log2 units). tW addresses the
+// lane quarter at column jb = 32*(warp&1); the lane's window starts at jb + lane + 48 - 16C.
+template <int C>
+__device__ __forceinline__ void rw_block(uint32_t tW, int lane, float (&blk)[16]) {
+  using namespace sm100;
+  uint32_t a[48];
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    uint32_t v[16];
+    tmem_ld16(tW + 48 - 16 * C + 16 * b, v);
+    tmem_wait_ld_regs(v);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) a[16 * b + e] = v[e];
+  }
+  shift_stage<4, 31>(a, lane);
+  shift_stage<3, 23>(a, lane);
+  shift_stage<2, 19>(a, lane);
+  shift_stage<1, 17>(a, lane);
+  shift_stage<0, 16>(a, lane);
+  // a[e] = RW[r][j + 48 - 16C + e] = rw[kw] with kw = 15 + 16C - e
+#pragma unroll
+  for (int e = 0; e < 16; ++e) blk[15 - e] = __uint_as_float(a[e]) * kLog2e;
+}
+
+// Hands block C (rw[16C .. 16C+15] of every lane's row) to the 16x256b owners: the thread keeps
+// rwA[m] = (rw[8m + 2c], rw[8m + 2c + 1]) of row srcA and rwB[m] of row srcA + 8, for m = 2C, 2C+1.
+template <int C>
+__device__ __forceinline__ void rw_scatter(const float (&blk)[16], int srcA, int c, float2 (&rwA)[8],
+                                           float2 (&rwB)[8]) {
+#pragma unroll
+  for (int mm = 0; mm < 2; ++mm) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float va = 0.f, vb = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const float sa = __shfl_sync(0xffffffffu, blk[8 * mm + 2 * cc + e], srcA);
+        const float sb = __shfl_sync(0xffffffffu, blk[8 * mm + 2 * cc + e], srcA + 8);
+        va = cc == c ? sa : va;
+        vb = cc == c ? sb : vb;
+      }
+      if (e == 0) {
+        rwA[2 * C + mm].x = va;
+        rwB[2 * C + mm].x = vb;
+      } else {
+        rwA[2 * C + mm].y = va;
+        rwB[2 * C + mm].y = vb;
+      }
+    }
+  }
+}
+
+// rh_park[kh][prow] = RH[OFF + 63 - kh] (log2 units) for the kh whose column OFF + 63 - kh lies in block B
+// (columns 32B .. 32B+31, held in v).
+template <int OFF, int B>
+__device__ __forceinline__ void park_rh(const uint32_t (&v)[32], float* rh_park, int prow) {
+#pragma unroll
+  for (int cc = 0; cc < 32; ++cc) {
+    const int kh = OFF + 63 - (32 * B + cc);
+    if (kh >= 0 && kh < 64) rh_park[kh * 256 + prow] = __uint_as_float(v[cc]) * kLog2e;
+  }
+}
+template <int OFF>
+__device__ __forceinline__ void park_rh_all(uint32_t tRH, float* rh_park, int prow) {
+  using namespace sm100;
+  uint32_t v[32];
+  tmem_ld32(tRH, v);
+  tmem_wait_ld_regs(v);
+  park_rh<OFF, 0>(v, rh_park, prow);
+  tmem_ld32(tRH + 32, v);
+  tmem_wait_ld_regs(v);
+  park_rh<OFF, 1>(v, rh_park, prow);
+  tmem_ld32(tRH + 64, v);
+  tmem_wait_ld_regs(v);
+  park_rh<OFF, 2>(v, rh_park, prow);
+}
+
+// Key block g = 0..15 of a tile holds keys 8g..8g+7 (64-key half g/8, rw index g%8); this thread's keys
+// in it are the pair 8g + 2c, +1 for rows A and B. A chunk = blocks G0, G0+1, loaded with 16x256b.x2:
+// v[4i], v[4i+1] row A and v[4i+2], v[4i+3] row B of block G0+i.
+
+// Pass 1: running maxima of S*c + rw for rows A and B.
+template <int G0>
+__device__ __forceinline__ void chunk_max(const uint32_t (&v)[8], float2 c2, const float2 (&rwA)[8],
+                                          const float2 (&rwB)[8], float& mA, float& mB) {
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int m = (G0 + i) & 7;
+    const float2 xa = sm100::fma2(make_float2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), c2, rwA[m]);
+    const float2 xb =
+        sm100::fma2(make_float2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])), c2, rwB[m]);
+    mA = sm100::max3(mA, xa.x, xa.y);
+    mB = sm100::max3(mB, xb.x, xb.y);
+  }
+}
+
+// Pass 2: p = 2^(S*c + rw + (rh - m)) for both rows, pair sums, and the 16-bit pairs in the 16x128b store
+// order (pw[2i] row A, pw[2i+1] row B: P column 4(G0+i) + c = keys 8(G0+i) + 2c, +1). Staged (exponents,
+// then the ex2, then sums and packing) so the ex2 issue back to back.
+template <int G0, bool BF16>
+__device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, const float2 (&rwA)[8],
+                                          const float2 (&rwB)[8], float2 bA, float2 bB, float2& sA, float2& sB,
+                                          uint32_t (&pw)[4]) {
+  float x[8];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int m = (G0 + i) & 7;
+    const float2 xa = sm100::fma2(make_float2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), c2,
+                                  sm100::add2(rwA[m], bA));
+    const float2 xb = sm100::fma2(make_float2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])), c2,
+                                  sm100::add2(rwB[m], bB));
+    x[4 * i] = xa.x;
+    x[4 * i + 1] = xa.y;
+    x[4 * i + 2] = xb.x;
+    x[4 * i + 3] = xb.y;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = sm100::ex2(x[i]);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    sA = sm100::add2(sA, make_float2(x[4 * i], x[4 * i + 1]));
+    sB = sm100::add2(sB, make_float2(x[4 * i + 2], x[4 * i + 3]));
+    pw[2 * i] = sm100::pack2(x[4 * i], x[4 * i + 1], BF16);
+    pw[2 * i + 1] = sm100::pack2(x[4 * i + 2], x[4 * i + 3], BF16);
+  }
+}
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    relpos_attn_global(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmT,
+                       T* __restrict__ out, float scale) {
+  using L = Layout<HD>;
+  using namespace sm100;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + L::OFF_BAR);
+  float* rh_park = reinterpret_cast<float*>(smem + L::OFF_RH);
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (device_faulted()) return;  // an earlier CTA reported a fault: do no more work
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long bh = blockIdx.x / (kN / 256);
+  const int ct = blockIdx.x % (kN / 256);
+  const int row0 = ct * 256;  // first query row of the CTA
+  const int I0 = ct * 4;      // its first grid row
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->pro_done, 1);
+    mbar_init(&bars->final_mma, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(&bars->bias_done[q], 8);  // one arrival per softmax warp of the query tile
+      mbar_init(&bars->s_full[q], 1);
+      mbar_init(&bars->p_full[q], 8);
+      mbar_init(&bars->o_done[q], 1);
+    }
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  if (warp < 4) {
+    regs_dec<kRegsLow>();
+    if (warp == 0) {
+      // ---------------------------------------------------------------- TMA producer
+      if (lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        tma_prefetch_desc(&tmT);
+        mbar_arrive_expect_tx(&bars->q_full, 4 * L::kQBytes);
+        for (int q = 0; q < 2; ++q)
+          for (int c = 0; c < L::HC; ++c)
+            tma_load_2d(smem + L::OFF_Q + q * L::kQBytes + c * L::kChunkBytes, &tmQ, &bars->q_full, c * 16,
+                        (int)(bh * kN + row0 + q * kBQ));
+        for (int c = 0; c < L::HC; ++c) {
+          tma_load_2d(smem + L::OFF_TH + c * L::kChunkBytes, &tmT, &bars->q_full, c * 16, I0);             // Th[I0..]
+          tma_load_2d(smem + L::OFF_TW + c * L::kChunkBytes, &tmT, &bars->q_full, c * 16, 2 * kSide - 1);  // Tw
+        }
+        int issued_k = 0, issued_v = 0;
+        for (int j = 0; j < kNT; ++j) {
+          const int st = j % kStages;
+          const uint32_t prev = ((j / kStages) - 1) & 1;
+          if (j >= kStages && !mbar_wait(&bars->k_empty[st], prev, abort_flag)) break;
+          mbar_arrive_expect_tx(&bars->k_full[st], L::kKBytes);
+          for (int a = 0; a < 2; ++a)
+            tma_load_2d(smem + L::OFF_K + st * L::kKBytes + a * L::kKAtom, &tmK, &bars->k_full[st],
+                        j * kBK + a * 64, (int)(bh * HD));
+          issued_k = j + 1;
+          if (j >= kStages && !mbar_wait(&bars->v_empty[st], prev, abort_flag)) break;
+          mbar_arrive_expect_tx(&bars->v_full[st], L::kVBytes);
+          for (int c = 0; c < L::HC; ++c)
+            tma_load_2d(smem + L::OFF_V + st * L::kVBytes + c * L::kChunkBytes, &tmV, &bars->v_full[st], c * 16,
+                        (int)(bh * kN + j * kBK));
+          issued_v = j + 1;
+        }
+        if (*abort_flag) {
+          // drain this CTA's own copies still in flight before the CTA can exit
+          for (int j = issued_k > kStages ? issued_k - kStages : 0; j < issued_k; ++j)
+            mbar_drain(&bars->k_full[j % kStages], (j / kStages) & 1);
+          for (int j = issued_v > kStages ? issued_v - kStages : 0; j < issued_v; ++j)
+            mbar_drain(&bars->v_full[j % kStages], (j / kStages) & 1);
+        }
+      }
+    } else if (warp == 1) {
+      // ---------------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idS = idesc_f16(kBf16, 128, 128, false, true);    // S = Q K^T, K MN-major
+        constexpr uint32_t idRW = idesc_f16(kBf16, 128, 128, false, false);  // RW = Q Tw^T
+        constexpr uint32_t idRH = idesc_f16(kBf16, 128, 80, false, false);   // RH = Q Th^T
+        constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);    // O += P V, V MN-major
+        const uint32_t sb = smem_u32(smem);
+        const uint64_t dQ = smem_desc(sb + L::OFF_Q, 16, 256, kLayoutSw32);
+        const uint64_t dTh = smem_desc(sb + L::OFF_TH, 16, 256, kLayoutSw32);
+        const uint64_t dTw = smem_desc(sb + L::OFF_TW, 16, 256, kLayoutSw32);
+        const uint64_t dK = smem_desc(sb + L::OFF_K, L::kKAtom, 1024, kLayoutSw128);
+        const uint64_t dV = smem_desc(sb + L::OFF_V, L::kChunkBytes, 256, kLayoutSw32);
+        // S_q from K stage st into the S_q columns
+        auto issue_s = [&](int q, int st) {
+          const uint64_t dKs = desc_add(dK, st * L::kKBytes);
+#pragma unroll
+          for (int c = 0; c < L::HC; ++c)
+            mma_ss(tmem + q * 128, desc_add(dQ, q * L::kQBytes + c * L::kChunkBytes), desc_add(dKs, c * 2048), idS,
+                   c > 0);
+        };
+        bool okk = mbar_wait(&bars->q_full, 0, abort_flag);
+        if (okk) {
+          tc_fence_after();
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+#pragma unroll
+            for (int c = 0; c < L::HC; ++c)
+              mma_ss(tmem + q * 128, desc_add(dQ, q * L::kQBytes + c * L::kChunkBytes),
+                     desc_add(dTw, c * L::kChunkBytes), idRW, c > 0);
+#pragma unroll
+            for (int c = 0; c < L::HC; ++c)
+              mma_ss(tmem + 256 + q * 80, desc_add(dQ, q * L::kQBytes + c * L::kChunkBytes),
+                     desc_add(dTh, c * L::kChunkBytes), idRH, c > 0);
+          }
+          mma_commit(&bars->pro_done);
+          // S_q overwrites RW_q and the rh park aliases the tables: both query tiles must be done with them
+          okk = mbar_wait(&bars->bias_done[0], 0, abort_flag) && mbar_wait(&bars->bias_done[1], 0, abort_flag) &&
+                mbar_wait(&bars->k_full[0], 0, abort_flag);
+        }
+        if (okk) {
+          tc_fence_after();
+          issue_s(0, 0);
+          mma_commit(&bars->s_full[0]);
+          issue_s(1, 0);
+          mma_commit(&bars->s_full[1]);
+          mma_commit(&bars->k_empty[0]);
+        }
+        for (int j = 0; j < kNT && okk; ++j) {
+          const int st = j % kStages, st1 = (j + 1) % kStages;
+          const uint64_t dVs = desc_add(dV, st * L::kVBytes);
+          const uint32_t acc0 = j > 0 ? 1u : 0u;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            okk = mbar_wait(&bars->p_full[q], j & 1, abort_flag);
+            if (okk && q == 0) okk = mbar_wait(&bars->v_full[st], (j / kStages) & 1, abort_flag);
+            if (!okk) break;
+            tc_fence_after();
+#pragma unroll
+            for (int s = 0; s < kBK / 16; ++s)
+              mma_ts(tmem + 256 + q * HD, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV, s > 0 ? 1u : acc0);
+            if (j + 1 < kNT) {
+              // issued after PV_q(j), which reads P_q(j) from the same columns: in-order execution
+              if (q == 0) {
+                okk = mbar_wait(&bars->k_full[st1], ((j + 1) / kStages) & 1, abort_flag);
+                if (!okk) break;
+                tc_fence_after();
+              }
+              issue_s(q, st1);
+              mma_commit(&bars->s_full[q]);
+            } else {
+              mma_commit(&bars->o_done[q]);
+            }
+          }
+          if (!okk) break;
+          mma_commit(&bars->v_empty[st]);
+          if (j + 1 < kNT) mma_commit(&bars->k_empty[st1]);
+        }
+        // every MMA issued by this thread has completed before the CTA tears down TMEM
+        mma_commit(&bars->final_mma);
+        mbar_drain(&bars->final_mma, 0);
+      }
+    }
+  } else {
+    regs_inc<kRegsHigh>();
+    // ------------------------------------------------------------------ softmax warps
+    const int sw = warp - 4;
+    const int q = sw >> 3;                // query tile
+    const int hh = (sw >> 2) & 1;         // 16-lane half of the lane quarter
+    const int wq = warp & 3;              // TMEM lane quarter
+    const int c = lane & 3;               // key-pair column within each 8-key block
+    const int lb = 32 * wq + 16 * hh;     // first TMEM lane (tile row) of this warp
+    const int rA = lb + (lane >> 2);      // this thread's rows rA and rA + 8 within the tile
+    const int prowA = q * 128 + rA, prowB = prowA + 8;
+    const uint32_t tS = tmem + ((uint32_t)lb << 16) + q * 128;
+    const uint32_t tO = tmem + ((uint32_t)lb << 16) + 256 + q * HD;
+    const float c_log2 = scale * kLog2e;
+    const float2 c2 = make_float2(c_log2, c_log2);
+    float2 rwA[8], rwB[8];
+    bool okk = __all_sync(0xffffffffu, mbar_wait(&bars->pro_done, 0, abort_flag));
+    if (okk) {
+      tc_fence_after();
+      const uint32_t tQuarter = tmem + ((uint32_t)(32 * wq) << 16);
+      // rh (one warp per lane quarter, 32x32b): RH_q[r][c'] = q_r . Th[I0 + c']. Row r of tile q sits on
+      // grid row i = I0 + 2q + r/64, so rh[kh] = q_r . Th[i - kh + 63] = RH_q[r][off + 63 - kh] with
+      // off = 2q + r/64 (warp-uniform). The park aliases the tables, which only the prologue MMAs read
+      // (they completed before pro_done).
+      if (hh == 0) {
+        const uint32_t tRH = tQuarter + 256 + q * 80;
+        const int prow = q * 128 + 32 * wq + lane;
+        switch (2 * q + (wq >> 1)) {
+          case 0:
+            park_rh_all<0>(tRH, rh_park, prow);
+            break;
+          case 1:
+            park_rh_all<1>(tRH, rh_park, prow);
+            break;
+          case 2:
+            park_rh_all<2>(tRH, rh_park, prow);
+            break;
+          default:
+            park_rh_all<3>(tRH, rh_park, prow);
+            break;
+        }
+      }
+      // rw: row r = 32wq + lane of the quarter has j = 32*(wq&1) + lane; its window RW[r][j .. j+63]
+      // reversed is rw[0..63]. Blocks of 16 are built per lane, then shuffled to the 16x256b owners.
+      {
+        const uint32_t tW = tQuarter + q * 128 + 32 * (wq & 1);
+        const int srcA = 16 * hh + (lane >> 2);
+        float blk[16];
+        rw_block<0>(tW, lane, blk);
+        rw_scatter<0>(blk, srcA, c, rwA, rwB);
+        rw_block<1>(tW, lane, blk);
+        rw_scatter<1>(blk, srcA, c, rwA, rwB);
+        rw_block<2>(tW, lane, blk);
+        rw_scatter<2>(blk, srcA, c, rwA, rwB);
+        rw_block<3>(tW, lane, blk);
+        rw_scatter<3>(blk, srcA, c, rwA, rwB);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->bias_done[q]);
+    }
+    float mrA = -INFINITY, mrB = -INFINITY, lA = 0.f, lB = 0.f;
+    for (int j = 0; j < kNT && okk; ++j) {
+      okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
+      if (!okk) break;
+      tc_fence_after();
+      const float rhA0 = rh_park[(2 * j) * 256 + prowA], rhA1 = rh_park[(2 * j + 1) * 256 + prowA];
+      const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
+      // pass 1: row maxima of S*c + rw + rh (rh per 64-key half), then across the row's four threads
+      float tA, tB;
+      {
+        uint32_t v0[8], v1[8];
+        float mA[2] = {-INFINITY, -INFINITY}, mB[2] = {-INFINITY, -INFINITY};
+        static_for<0, 4>([&](auto kk) {
+          constexpr int k = decltype(kk)::value;  // chunks 2k and 2k+1 = blocks 4k .. 4k+3
+          tmem_ld_16x256b_x2(tS + 32 * k, v0);
+          tmem_ld_16x256b_x2(tS + 32 * k + 16, v1);
+          tmem_wait_ld_regs(v0);
+          tmem_wait_ld_regs(v1);
+          chunk_max<4 * k>(v0, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
+          chunk_max<4 * k + 2>(v1, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
+        });
+        tA = fmaxf(mA[0] + rhA0, mA[1] + rhA1);
+        tB = fmaxf(mB[0] + rhB0, mB[1] + rhB1);
+        tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 1));
+        tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 1));
+        tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 2));
+        tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 2));
+      }
+      const bool needA = (j == 0) || (tA > mrA + kRescaleThreshold);
+      const bool needB = (j == 0) || (tB > mrB + kRescaleThreshold);
+      float alA = 1.f, alB = 1.f;
+      if (needA) {
+        const float mn = fmaxf(mrA, tA);
+        alA = ex2(mrA - mn);
+        mrA = mn;
+      }
+      if (needB) {
+        const float mn = fmaxf(mrB, tB);
+        alB = ex2(mrB - mn);
+        mrB = mn;
+      }
+      // pass 2: p = 2^(S*c + rw + rh - m); P of chunk k (16-bit pairs, columns 8k..8k+7) lands on scores of
+      // chunk k/2 <= k, already read. The load of chunk k+1 is in flight meanwhile.
+      float2 sA = make_float2(0.f, 0.f), sB = make_float2(0.f, 0.f);
+      {
+        const float2 bA0 = make_float2(rhA0 - mrA, rhA0 - mrA), bA1 = make_float2(rhA1 - mrA, rhA1 - mrA);
+        const float2 bB0 = make_float2(rhB0 - mrB, rhB0 - mrB), bB1 = make_float2(rhB1 - mrB, rhB1 - mrB);
+        uint32_t v0[8], v1[8], pw[4];
+        tmem_ld_16x256b_x2(tS + 0, v0);
+        tmem_wait_ld_regs(v0);
+        static_for<0, 8>([&](auto kk) {
+          constexpr int k = decltype(kk)::value;  // chunk k = blocks 2k, 2k+1
+          uint32_t(&cur)[8] = (k & 1) ? v1 : v0;
+          uint32_t(&nxt)[8] = (k & 1) ? v0 : v1;
+          if constexpr (k + 1 < 8) tmem_ld_16x256b_x2(tS + 16 * (k + 1), nxt);
+          if constexpr (k < 4)
+            chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA0, bB0, sA, sB, pw);
+          else
+            chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA1, bB1, sA, sB, pw);
+          tmem_st_16x128b_x2(tS + 8 * k, pw);
+          if constexpr (k + 1 < 8) tmem_wait_ld_regs(nxt);
+        });
+      }
+      lA = lA * alA + (sA.x + sA.y);  // this thread's share of the row sum (combined in the epilogue)
+      lB = lB * alB + (sB.x + sB.y);
+      // O rescale: PV_q(j-1) has completed (it was issued before S_q(j), whose commit we waited on).
+      if (__any_sync(0xffffffffu, (needA || needB) && j > 0)) {
+#pragma unroll
+        for (int c0 = 0; c0 < HD; c0 += 16) {
+          uint32_t ov[8];
+          tmem_ld_16x256b_x2(tO + c0, ov);
+          tmem_wait_ld_regs(ov);
+          ov[0] = __float_as_uint(__uint_as_float(ov[0]) * alA);
+          ov[1] = __float_as_uint(__uint_as_float(ov[1]) * alA);
+          ov[4] = __float_as_uint(__uint_as_float(ov[4]) * alA);
+          ov[5] = __float_as_uint(__uint_as_float(ov[5]) * alA);
+          ov[2] = __float_as_uint(__uint_as_float(ov[2]) * alB);
+          ov[3] = __float_as_uint(__uint_as_float(ov[3]) * alB);
+          ov[6] = __float_as_uint(__uint_as_float(ov[6]) * alB);
+          ov[7] = __float_as_uint(__uint_as_float(ov[7]) * alB);
+          tmem_st_16x256b_x2(tO + c0, ov);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();  // every lane's P and O stores are complete: one arrival per warp
+      if (lane == 0) mbar_arrive(&bars->p_full[q]);
+    }
+    // epilogue: O / l -> out, once PV_q of the last tile has completed
+    if (okk) okk = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[q], 0, abort_flag));
+    if (okk) {
+      tc_fence_after();
+      lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+      lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+      lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+      lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+      const float invA = 1.f / lA, invB = 1.f / lB;
+      T* oA = out + (bh * kN + row0 + prowA) * HD + 2 * c;
+      T* oB = oA + 8 * HD;
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 16) {
+        uint32_t ov[8];
+        tmem_ld_16x256b_x2(tO + c0, ov);
+        tmem_wait_ld_regs(ov);
+        *reinterpret_cast<uint32_t*>(oA + c0) =
+            pack2(__uint_as_float(ov[0]) * invA, __uint_as_float(ov[1]) * invA, kBf16);
+        *reinterpret_cast<uint32_t*>(oA + c0 + 8) =
+            pack2(__uint_as_float(ov[4]) * invA, __uint_as_float(ov[5]) * invA, kBf16);
+        *reinterpret_cast<uint32_t*>(oB + c0) =
+            pack2(__uint_as_float(ov[2]) * invB, __uint_as_float(ov[3]) * invB, kBf16);
+        *reinterpret_cast<uint32_t*>(oB + c0 + 8) =
+            pack2(__uint_as_float(ov[6]) * invB, __uint_as_float(ov[7]) * invB, kBf16);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tcg
+}  // namespace samrs
