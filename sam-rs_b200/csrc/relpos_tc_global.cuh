@@ -208,8 +208,14 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, con
     x[4 * i + 2] = xb.x;
     x[4 * i + 3] = xb.y;
   }
+  // 6 of the 8 exponentials on the exp unit, the row-B pair of the second block on the FMA pipe
 #pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = sm100::ex2(x[i]);
+  for (int i = 0; i < 6; ++i) x[i] = sm100::ex2(x[i]);
+  {
+    const float2 pe = sm100::ex2_poly2(make_float2(x[6], x[7]));
+    x[6] = pe.x;
+    x[7] = pe.y;
+  }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     sA = sm100::add2(sA, make_float2(x[4 * i], x[4 * i + 1]));
@@ -365,7 +371,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             okk = mbar_wait(&bars->p_full[q], j & 1, abort_flag);
+            // the operands of this tile and of the next S: waited on before the MMA run, so that PV_q(j) and
+            // S_q(j+1) issue back to back
             if (okk && q == 0) okk = mbar_wait(&bars->v_full[st], (j / kStages) & 1, abort_flag);
+            if (okk && q == 0 && j + 1 < kNT) okk = mbar_wait(&bars->k_full[st1], ((j + 1) / kStages) & 1, abort_flag);
             if (!okk) break;
             tc_fence_after();
 #pragma unroll
@@ -373,11 +382,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               mma_ts(tmem + 256 + q * HD, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV, s > 0 ? 1u : acc0);
             if (j + 1 < kNT) {
               // issued after PV_q(j), which reads P_q(j) from the same columns: in-order execution
-              if (q == 0) {
-                okk = mbar_wait(&bars->k_full[st1], ((j + 1) / kStages) & 1, abort_flag);
-                if (!okk) break;
-                tc_fence_after();
-              }
               issue_s(q, st1);
               mma_commit(&bars->s_full[q]);
             } else {

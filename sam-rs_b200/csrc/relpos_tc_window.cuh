@@ -21,10 +21,11 @@
 // dims per 128-byte core matrix). The table rows are written into both K buffers once, at start-up.
 // Rings: Q+K (2 stages, released when a unit's S MMAs complete) and V (2 stages, released after PV).
 //
-// Warps: 0 TMA producer, 1 MMA issuer, 2-3 kt loaders (warp 2 also allocates TMEM), 4-7 / 8-11 softmax +
-// epilogue of query tile 0 / 1 (thread = query row = TMEM lane); warp 11 covers rows 224..255 only,
-// which are all padding, so it only keeps the barrier counts.
-// The MMA issue order keeps the two tiles half a unit apart: S0(u) PV1(u-1) S1(u) PV0(u) S0(u+1) ...
+// Warps: 0 / 1 MMA issuers of query tile 1 / 0 (one thread each, so the two tiles' S -> softmax -> PV ->
+// epilogue chains never wait on each other), 2-3 kt loaders (thread 0 of warp 2 also issues the q and v
+// TMA loads; warp 2 allocates TMEM), 4-7 / 8-11 softmax + epilogue of query tile 0 / 1 (thread = query
+// row = TMEM lane); warp 11 covers rows 224..255 only, which are all padding, so it only keeps the
+// barrier counts.
 // TMEM (512 columns): tile t owns [256t, 256t+256): S_t; then P_t (16-bit pairs, cols 0..103) written
 // over the consumed scores; O_t accumulates in cols [128, 128+hd) once the softmax has consumed S_t.
 #pragma once
@@ -69,11 +70,7 @@ struct Layout {
   static constexpr int OFF_Q = 0, OFF_K = kQBytes;  // within a QK stage
   static constexpr int OFF_V = kStages * kQKStage;
   static constexpr int OFF_BAR = OFF_V + kStages * kVStage;
-  // output staging: one [16 rows x HD] block per TMEM lane quarter, shared by the two tiles' warps
-  static constexpr int kStgRows = 16;
-  static constexpr int kStgBytes = kStgRows * HD * 2;
-  static constexpr int OFF_STG = OFF_BAR + 256;
-  static constexpr int kSmemBytes = OFF_STG + 4 * kStgBytes + 1024;
+  static constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
   static_assert(kQChunk % 256 == 0 && kVChunk % 256 == 0 && OFF_K % 128 == 0 && kQKStage % 256 == 0, "alignment");
   static_assert((256 - kQRows) * 32 <= kKBytes, "tile-1 over-read stays inside the stage");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -81,9 +78,8 @@ struct Layout {
 
 struct Bars {
   uint64_t q_full[kStages], v_full[kStages], k_full[kStages], qk_free[kStages], v_free[kStages];
-  uint64_t final_mma;
+  uint64_t final_mma[2];
   uint64_t s_full[2], p_full[2], o_full[2], t_free[2];
-  uint64_t stg_to0[4], stg_to1[4];  // staging buffer handed to tile 0's / tile 1's warp
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -138,14 +134,33 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&sv)[32], float2 c2, c
 template <int CH, int NE, bool BF16>
 __device__ __forceinline__ void chunk_exp(const uint32_t (&sv)[32], float2 c2, const Bias& b, float2 (&sum)[4],
                                           uint32_t (&pk)[16]) {
+  // Staged: all exponents, then the exponentials (one pair in four on the FMA pipe), then sums and packing.
+  constexpr int NV = (32 * CH + NE <= kN) ? NE : (kN - 32 * CH);  // keys of the chunk below kN (even)
+  float x[32];
+#pragma unroll
+  for (int e = 0; e < NV; e += 2) {
+    const int k0 = 32 * CH + e;
+    const float2 s2 = make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+    const float2 t = sm100::add2(sm100::fma2(s2, c2, b.rhp[k0 / kSide]), b.rwp[(k0 % kSide) >> 1]);
+    x[e] = t.x;
+    x[e + 1] = t.y;
+  }
+#pragma unroll
+  for (int e = 0; e < NV; e += 2) {
+    if ((e & 6) == 6) {
+      const float2 p = sm100::ex2_poly2(make_float2(x[e], x[e + 1]));
+      x[e] = p.x;
+      x[e + 1] = p.y;
+    } else {
+      x[e] = sm100::ex2(x[e]);
+      x[e + 1] = sm100::ex2(x[e + 1]);
+    }
+  }
 #pragma unroll
   for (int e = 0; e < NE; e += 2) {
-    const int k0 = 32 * CH + e;
     float2 p = make_float2(0.f, 0.f);
-    if (k0 < kN) {
-      const float2 s2 = make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
-      const float2 x = sm100::add2(sm100::fma2(s2, c2, b.rhp[k0 / kSide]), b.rwp[(k0 % kSide) >> 1]);
-      p = make_float2(sm100::ex2(x.x), sm100::ex2(x.y));
+    if (e < NV) {
+      p = make_float2(x[e], x[e + 1]);
       sum[(e >> 1) & 3] = sm100::add2(sum[(e >> 1) & 3], p);
     }
     pk[e >> 1] = sm100::pack2(p.x, p.y, BF16);
@@ -274,19 +289,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->q_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->k_full[s], kLoaders);
-      mbar_init(&bars->qk_free[s], 1);
-      mbar_init(&bars->v_free[s], 1);
+      mbar_init(&bars->qk_free[s], 2);  // one commit per tile issuer
+      mbar_init(&bars->v_free[s], 2);
     }
-    mbar_init(&bars->final_mma, 1);
+    mbar_init(&bars->final_mma[0], 1);
+    mbar_init(&bars->final_mma[1], 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars->s_full[t], 1);
-      mbar_init(&bars->p_full[t], 128);
+      mbar_init(&bars->p_full[t], 4);  // one arrival per softmax warp of the tile
       mbar_init(&bars->o_full[t], 1);
-      mbar_init(&bars->t_free[t], 128);
-    }
-    for (int w = 0; w < 4; ++w) {
-      mbar_init(&bars->stg_to0[w], 1);
-      mbar_init(&bars->stg_to1[w], 1);
+      mbar_init(&bars->t_free[t], 4);
     }
     bars->abort_flag = 0;
     fence_mbar_init();
@@ -302,92 +314,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < 4) {
     regs_dec<kRegsLow>();
-    if (warp == 0) {
-      // ---------------------------------------------------------------- TMA producer (q, v)
+    if (warp < 2) {
+      // ---------------------------------------------------------------- MMA issuer of tile t
       if (lane == 0) {
-        tma_prefetch_desc(&tmQ);
-        tma_prefetch_desc(&tmV);
-        int issued = 0;
-        for (int ui = 0; ui < n_units; ++ui) {
-          const int s = ui & 1;
-          const int u = (int)(first + (long)ui * gridDim.x);
-          const uint32_t prev = ((ui >> 1) - 1) & 1;
-          if (ui >= kStages && !mbar_wait(&bars->qk_free[s], prev, abort_flag)) break;
-          mbar_arrive_expect_tx(&bars->q_full[s], L::kQBytes);
-          for (int c = 0; c < L::HC; ++c)
-            tma_load_3d(smem + s * L::kQKStage + L::OFF_Q + c * L::kQChunk, &tmQ, &bars->q_full[s], c * 16, 0, u);
-          if (ui >= kStages && !mbar_wait(&bars->v_free[s], prev, abort_flag)) break;
-          mbar_arrive_expect_tx(&bars->v_full[s], L::kVBytes);
-          for (int c = 0; c < L::HC; ++c)
-            tma_load_3d(smem + L::OFF_V + s * L::kVStage + c * L::kVChunk, &tmV, &bars->v_full[s], c * 16, 0, u);
-          issued = ui + 1;
-        }
-        if (*abort_flag) {
-          for (int ui = issued > kStages ? issued - kStages : 0; ui < issued; ++ui) {
-            mbar_drain(&bars->q_full[ui & 1], (ui >> 1) & 1);
-            mbar_drain(&bars->v_full[ui & 1], (ui >> 1) & 1);
-          }
-        }
-      }
-    } else if (warp == 1) {
-      // ---------------------------------------------------------------- MMA issuer
-      if (lane == 0) {
+        const int t = 1 - warp;
         constexpr uint32_t idS = idesc_f16(kBf16, 128, kNB, false, true);
         constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);
         const uint32_t sb = smem_u32(smem);
-        auto smma = [&](int s, int t) {
-          const uint32_t qa = sb + s * L::kQKStage + L::OFF_Q + t * 128 * 32;
-          const uint32_t kb = sb + s * L::kQKStage + L::OFF_K;
-          for (int c = 0; c < L::HC; ++c)
-            mma_ss(tmem + 256 * t, smem_desc(qa + c * L::kQChunk, 16, 256, kLayoutSw32),
-                   smem_desc(kb + c * 256, 128, L::kKSbo, kLayoutNone), idS, c > 0);
-          mma_commit(&bars->s_full[t]);
-        };
-        auto pv = [&](int s, int t) {
-          const uint32_t vb = sb + L::OFF_V + s * L::kVStage;
-          for (int k = 0; k < kNP / 16; ++k)
-            mma_ts(tmem + 256 * t + 128, tmem + 256 * t + 8 * k, smem_desc(vb + k * 512, L::kVChunk, 256, kLayoutSw32),
-                   idPV, k > 0 ? 1u : 0u);
-          mma_commit(&bars->o_full[t]);
-        };
+        const uint64_t dQ = smem_desc(sb + L::OFF_Q + t * 128 * 32, 16, 256, kLayoutSw32);
+        const uint64_t dK = smem_desc(sb + L::OFF_K, 128, L::kKSbo, kLayoutNone);
+        const uint64_t dV = smem_desc(sb + L::OFF_V, L::kVChunk, 256, kLayoutSw32);
+        const uint32_t tT = tmem + 256 * t;
         bool okk = true;
-        // Issue order: S0(u) | PV1(u-1) | S1(u) | PV0(u) | S0(u+1) ...
         for (int ui = 0; ui < n_units && okk; ++ui) {
-          const int s = ui & 1, sp = s ^ 1;
+          const int s = ui & 1;
           const uint32_t ph = (ui >> 1) & 1;
+          // S_t(u) overwrites the tile's columns: the softmax warps must have read O_t(u-1)
           okk = mbar_wait(&bars->q_full[s], ph, abort_flag) && mbar_wait(&bars->k_full[s], ph, abort_flag) &&
-                (ui == 0 || mbar_wait(&bars->t_free[0], (ui - 1) & 1, abort_flag));
+                (ui == 0 || mbar_wait(&bars->t_free[t], (ui - 1) & 1, abort_flag));
           if (!okk) break;
           tc_fence_after();
-          smma(s, 0);
-          if (ui > 0) {
-            okk = mbar_wait(&bars->p_full[1], (ui - 1) & 1, abort_flag);
-            if (!okk) break;
-            tc_fence_after();
-            pv(sp, 1);
-            mma_commit(&bars->v_free[sp]);
-          }
-          okk = ui == 0 || mbar_wait(&bars->t_free[1], (ui - 1) & 1, abort_flag);
+#pragma unroll
+          for (int c = 0; c < L::HC; ++c)
+            mma_ss(tT, desc_add(dQ, s * L::kQKStage + c * L::kQChunk), desc_add(dK, s * L::kQKStage + c * 256), idS,
+                   c > 0);
+          mma_commit(&bars->s_full[t]);
+          mma_commit(&bars->qk_free[s]);  // this tile's reads of the unit's Q and K are done once S_t completes
+          okk = mbar_wait(&bars->v_full[s], ph, abort_flag) && mbar_wait(&bars->p_full[t], ui & 1, abort_flag);
           if (!okk) break;
           tc_fence_after();
-          smma(s, 1);
-          mma_commit(&bars->qk_free[s]);  // this unit's Q and K are no longer read once its S MMAs finish
-          okk = mbar_wait(&bars->v_full[s], ph, abort_flag) && mbar_wait(&bars->p_full[0], ui & 1, abort_flag);
-          if (!okk) break;
-          tc_fence_after();
-          pv(s, 0);
+#pragma unroll
+          for (int k = 0; k < kNP / 16; ++k)
+            mma_ts(tT + 128, tT + 8 * k, desc_add(dV, s * L::kVStage + k * 512), idPV, k > 0 ? 1u : 0u);
+          mma_commit(&bars->o_full[t]);
+          mma_commit(&bars->v_free[s]);
         }
-        if (okk && n_units > 0) {  // PV1 of the last unit
-          const int ul = n_units - 1;
-          okk = mbar_wait(&bars->p_full[1], ul & 1, abort_flag);
-          if (okk) {
-            tc_fence_after();
-            pv(ul & 1, 1);
-            mma_commit(&bars->v_free[ul & 1]);
-          }
-        }
-        mma_commit(&bars->final_mma);
-        mbar_drain(&bars->final_mma, 0);
+        mma_commit(&bars->final_mma[t]);
+        mbar_drain(&bars->final_mma[t], 0);
       }
     } else {
       // ---------------------------------------------------------------- kt loaders (cp.async relayout)
@@ -406,10 +369,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       // down kt by one 392-byte row per d, the destination by 16 bytes ((d/8)*128 + (d%8)*16 = 16 d).
       const int c = tl;
       const uint32_t dst0 = (uint32_t)((c >> 1) * L::kKSbo + (c & 1) * 8);
+      // Thread 0 also issues the unit's q (with its K) and v TMA loads.
+      if (tl == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmV);
+      }
+      int issued_q = 0, issued_v = 0;
       for (int ui = 0; ui < n_units; ++ui) {
         const int s = ui & 1;
         const long u = first + (long)ui * gridDim.x;
-        if (ui >= kStages && !mbar_wait(&bars->qk_free[s], ((ui >> 1) - 1) & 1, abort_flag)) break;
+        const uint32_t prev = ((ui >> 1) - 1) & 1;
+        if (ui >= kStages && !mbar_wait(&bars->qk_free[s], prev, abort_flag)) break;
+        if (tl == 0) {
+          mbar_arrive_expect_tx(&bars->q_full[s], L::kQBytes);
+          for (int cq = 0; cq < L::HC; ++cq)
+            tma_load_3d(smem + s * L::kQKStage + L::OFF_Q + cq * L::kQChunk, &tmQ, &bars->q_full[s], cq * 16, 0,
+                        (int)u);
+          issued_q = ui + 1;
+        }
         if (c < kN / 4) {
           uint8_t* dst = smem + s * L::kQKStage + L::OFF_K + dst0;
           const T* src = kt + u * (long)HD * kN + 4 * c;
@@ -419,8 +396,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         cp_async_wait_all();
         fence_proxy_async_smem();
         mbar_arrive(&bars->k_full[s]);
+        if (tl == 0) {
+          if (ui >= kStages && !mbar_wait(&bars->v_free[s], prev, abort_flag)) break;
+          mbar_arrive_expect_tx(&bars->v_full[s], L::kVBytes);
+          for (int cv = 0; cv < L::HC; ++cv)
+            tma_load_3d(smem + L::OFF_V + s * L::kVStage + cv * L::kVChunk, &tmV, &bars->v_full[s], cv * 16, 0,
+                        (int)u);
+          issued_v = ui + 1;
+        }
       }
       cp_async_wait_all();
+      if (tl == 0 && *abort_flag) {
+        // drain this CTA's own TMA copies still in flight before the CTA can exit
+        for (int ui = issued_q > kStages ? issued_q - kStages : 0; ui < issued_q; ++ui)
+          mbar_drain(&bars->q_full[ui & 1], (ui >> 1) & 1);
+        for (int ui = issued_v > kStages ? issued_v - kStages : 0; ui < issued_v; ++ui)
+          mbar_drain(&bars->v_full[ui & 1], (ui >> 1) & 1);
+      }
     }
   } else {
     regs_inc<kRegsHigh>();
@@ -433,7 +425,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tS = tmem + ((uint32_t)(32 * wq) << 16) + 256 * t;
     const uint32_t tO = tS + 128;
     const float c = scale * kLog2e;
-    uint8_t* stg = smem + L::OFF_STG + wq * L::kStgBytes;
     for (int ui = 0; ui < n_units; ++ui) {
       const long u = first + (long)ui * gridDim.x;
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[t], ui & 1, abort_flag))) break;
@@ -450,19 +441,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
       }
       tc_fence_before();
-      mbar_arrive(&bars->p_full[t]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[t]);
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_full[t], ui & 1, abort_flag))) break;
       tc_fence_after();
-      // Epilogue: O/l -> this warp's staging block, 16 rows at a time (row-major, i.e. the layout of
-      // those rows in `out`), then fully coalesced 16-byte stores. Tile 0 and tile 1 warps of the same
-      // lane quarter take the staging buffer in turn: tile 0 of unit u, tile 1 of unit u, tile 0 of u+1...
-      const bool turn_ok = t == 0 ? (ui == 0 || mbar_wait(&bars->stg_to0[wq], (ui - 1) & 1, abort_flag))
-                                  : mbar_wait(&bars->stg_to1[wq], ui & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, turn_ok)) break;
+      // Epilogue: O/l into registers, the tile's TMEM columns handed back at once (the next unit's S MMA
+      // may overwrite them), then the row's 16-byte stores.
+      uint32_t pw[HD / 16][8];
       if (live) {
         const float inv = 1.f / sum;
-        const int row0 = 128 * t + 32 * wq;
-        uint32_t pw[HD / 16][8];
 #pragma unroll
         for (int c0 = 0; c0 < HD / 16; ++c0) {
           uint32_t ov[16];
@@ -472,34 +459,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 8; ++e)
             pw[c0][e] = pack2(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv, kBf16);
         }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->t_free[t]);  // O_t read and S_t columns free for the next unit's S MMA
+      if (live && rt < kN) {
+        uint4* orow = reinterpret_cast<uint4*>(out + (u * kN + rt) * HD);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          if ((lane >> 4) == half) {
-#pragma unroll
-            for (int c0 = 0; c0 < HD / 16; ++c0) {
-              uint4* srow = reinterpret_cast<uint4*>(stg + (lane & 15) * (HD * 2) + 32 * c0);
-              srow[0] = make_uint4(pw[c0][0], pw[c0][1], pw[c0][2], pw[c0][3]);
-              srow[1] = make_uint4(pw[c0][4], pw[c0][5], pw[c0][6], pw[c0][7]);
-            }
-          }
-          __syncwarp();
-          const int hrow0 = row0 + 16 * half;
-          const int left = kN - hrow0;
-          const int nrows = left < L::kStgRows ? (left > 0 ? left : 0) : L::kStgRows;
-          const int nchunks = nrows * (HD / 8);  // 16-byte chunks of these rows
-          const uint4* sbuf = reinterpret_cast<const uint4*>(stg);
-          uint4* gdst = reinterpret_cast<uint4*>(out + (u * kN + hrow0) * HD);
-#pragma unroll
-          for (int k = 0; k < (L::kStgRows * HD / 8 + 31) / 32; ++k) {
-            const int ch = lane + 32 * k;
-            if (ch < nchunks) gdst[ch] = sbuf[ch];
-          }
-          __syncwarp();
+        for (int c0 = 0; c0 < HD / 16; ++c0) {
+          orow[2 * c0] = make_uint4(pw[c0][0], pw[c0][1], pw[c0][2], pw[c0][3]);
+          orow[2 * c0 + 1] = make_uint4(pw[c0][4], pw[c0][5], pw[c0][6], pw[c0][7]);
         }
       }
-      if (lane == 0) mbar_arrive(t == 0 ? &bars->stg_to1[wq] : &bars->stg_to0[wq]);
-      tc_fence_before();
-      mbar_arrive(&bars->t_free[t]);  // O_t read and S_t columns free for the next unit's S MMA
     }
   }
   tc_fence_before();
