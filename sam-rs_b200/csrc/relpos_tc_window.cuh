@@ -19,11 +19,13 @@
 // 392-byte row pitch, which TMA cannot tile (strides must be multiples of 16 B), so 64 loader threads
 // move it with 8-byte cp.async straight into the canonical no-swizzle MN-major UMMA layout (8 keys x 8
 // dims per 128-byte core matrix). The table rows are written into both K buffers once, at start-up.
-// Rings: Q+K (2 stages, released when a unit's S MMAs complete) and V (2 stages, released after PV).
+// Rings: Q+K (2 stages, released when a unit's S MMAs complete) and a single V stage (reloaded once both
+// tiles' PV MMAs completed; the load has the next unit's softmax to land). Output rows are staged in
+// shared memory and written back by one bulk store per warp.
 //
 // Warps: 0 / 1 MMA issuers of query tile 1 / 0 (one thread each, so the two tiles' S -> softmax -> PV ->
-// epilogue chains never wait on each other), 2-3 kt loaders (thread 0 of warp 2 also issues the q and v
-// TMA loads; warp 2 allocates TMEM), 4-7 / 8-11 softmax + epilogue of query tile 0 / 1 (thread = query
+// epilogue chains never wait on each other), 2-3 kt loaders (thread 0 also issues the q TMA loads, the
+// last thread the v TMA loads; warp 2 allocates TMEM), 4-7 / 8-11 softmax + epilogue of query tile 0 / 1 (thread = query
 // row = TMEM lane); warp 11 covers rows 224..255 only, which are all padding, so it only keeps the
 // barrier counts.
 // TMEM (512 columns): tile t owns [256t, 256t+256): S_t; then P_t (16-bit pairs, cols 0..103) written
@@ -68,8 +70,11 @@ struct Layout {
   static constexpr int kQKStage = (kQBytes + kKBytes + 255) / 256 * 256;
   static constexpr int kVStage = (kVBytes + 255) / 256 * 256;
   static constexpr int OFF_Q = 0, OFF_K = kQBytes;  // within a QK stage
-  static constexpr int OFF_V = kStages * kQKStage;
-  static constexpr int OFF_BAR = OFF_V + kStages * kVStage;
+  static constexpr int OFF_V = kStages * kQKStage;  // one V stage: loaded during the unit's softmax
+  // output staging: the 128 rows of each tile (row-major, as in `out`), written back by bulk stores
+  static constexpr int kStgTile = 128 * HD * 2;
+  static constexpr int OFF_STG = OFF_V + kVStage;
+  static constexpr int OFF_BAR = OFF_STG + 2 * kStgTile;
   static constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
   static_assert(kQChunk % 256 == 0 && kVChunk % 256 == 0 && OFF_K % 128 == 0 && kQKStage % 256 == 0, "alignment");
   static_assert((256 - kQRows) * 32 <= kKBytes, "tile-1 over-read stays inside the stage");
@@ -77,7 +82,7 @@ struct Layout {
 };
 
 struct Bars {
-  uint64_t q_full[kStages], v_full[kStages], k_full[kStages], qk_free[kStages], v_free[kStages];
+  uint64_t q_full[kStages], k_full[kStages], qk_free[kStages], v_full, v_free;
   uint64_t final_mma[2];
   uint64_t s_full[2], p_full[2], o_full[2], t_free[2];
   uint32_t tmem_base;
@@ -287,11 +292,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->q_full[s], 1);
-      mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->k_full[s], kLoaders);
-      mbar_init(&bars->qk_free[s], 2);  // one commit per tile issuer
-      mbar_init(&bars->v_free[s], 2);
+      mbar_init(&bars->k_full[s], kLoaders - 1);  // the last loader thread issues the v loads instead
+      mbar_init(&bars->qk_free[s], 2);            // one commit per tile issuer
     }
+    mbar_init(&bars->v_full, 1);
+    mbar_init(&bars->v_free, 2);
     mbar_init(&bars->final_mma[0], 1);
     mbar_init(&bars->final_mma[1], 1);
     for (int t = 0; t < 2; ++t) {
@@ -340,14 +345,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                    c > 0);
           mma_commit(&bars->s_full[t]);
           mma_commit(&bars->qk_free[s]);  // this tile's reads of the unit's Q and K are done once S_t completes
-          okk = mbar_wait(&bars->v_full[s], ph, abort_flag) && mbar_wait(&bars->p_full[t], ui & 1, abort_flag);
+          okk = mbar_wait(&bars->v_full, ui & 1, abort_flag) && mbar_wait(&bars->p_full[t], ui & 1, abort_flag);
           if (!okk) break;
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < kNP / 16; ++k)
-            mma_ts(tT + 128, tT + 8 * k, desc_add(dV, s * L::kVStage + k * 512), idPV, k > 0 ? 1u : 0u);
+            mma_ts(tT + 128, tT + 8 * k, desc_add(dV, k * 512), idPV, k > 0 ? 1u : 0u);
           mma_commit(&bars->o_full[t]);
-          mma_commit(&bars->v_free[s]);
+          mma_commit(&bars->v_free);
         }
         mma_commit(&bars->final_mma[t]);
         mbar_drain(&bars->final_mma[t], 0);
@@ -369,49 +374,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       // down kt by one 392-byte row per d, the destination by 16 bytes ((d/8)*128 + (d%8)*16 = 16 d).
       const int c = tl;
       const uint32_t dst0 = (uint32_t)((c >> 1) * L::kKSbo + (c & 1) * 8);
-      // Thread 0 also issues the unit's q (with its K) and v TMA loads.
-      if (tl == 0) {
-        tma_prefetch_desc(&tmQ);
+      if (tl == kLoaders - 1) {
+        // v loads: the single V stage is reloaded once both tiles' PV MMAs of the previous unit completed
         tma_prefetch_desc(&tmV);
-      }
-      int issued_q = 0, issued_v = 0;
-      for (int ui = 0; ui < n_units; ++ui) {
-        const int s = ui & 1;
-        const long u = first + (long)ui * gridDim.x;
-        const uint32_t prev = ((ui >> 1) - 1) & 1;
-        if (ui >= kStages && !mbar_wait(&bars->qk_free[s], prev, abort_flag)) break;
-        if (tl == 0) {
-          mbar_arrive_expect_tx(&bars->q_full[s], L::kQBytes);
-          for (int cq = 0; cq < L::HC; ++cq)
-            tma_load_3d(smem + s * L::kQKStage + L::OFF_Q + cq * L::kQChunk, &tmQ, &bars->q_full[s], cq * 16, 0,
-                        (int)u);
-          issued_q = ui + 1;
-        }
-        if (c < kN / 4) {
-          uint8_t* dst = smem + s * L::kQKStage + L::OFF_K + dst0;
-          const T* src = kt + u * (long)HD * kN + 4 * c;
-#pragma unroll 8
-          for (int d = 0; d < HD; ++d) cp_async_8(dst + 16 * d, src + d * kN);
-        }
-        cp_async_wait_all();
-        fence_proxy_async_smem();
-        mbar_arrive(&bars->k_full[s]);
-        if (tl == 0) {
-          if (ui >= kStages && !mbar_wait(&bars->v_free[s], prev, abort_flag)) break;
-          mbar_arrive_expect_tx(&bars->v_full[s], L::kVBytes);
+        int issued_v = 0;
+        for (int ui = 0; ui < n_units; ++ui) {
+          const long u = first + (long)ui * gridDim.x;
+          if (ui > 0 && !mbar_wait(&bars->v_free, (ui - 1) & 1, abort_flag)) break;
+          mbar_arrive_expect_tx(&bars->v_full, L::kVBytes);
           for (int cv = 0; cv < L::HC; ++cv)
-            tma_load_3d(smem + L::OFF_V + s * L::kVStage + cv * L::kVChunk, &tmV, &bars->v_full[s], cv * 16, 0,
-                        (int)u);
+            tma_load_3d(smem + L::OFF_V + cv * L::kVChunk, &tmV, &bars->v_full, cv * 16, 0, (int)u);
           issued_v = ui + 1;
         }
-      }
-      cp_async_wait_all();
-      if (tl == 0 && *abort_flag) {
-        // drain this CTA's own TMA copies still in flight before the CTA can exit
-        for (int ui = issued_q > kStages ? issued_q - kStages : 0; ui < issued_q; ++ui)
-          mbar_drain(&bars->q_full[ui & 1], (ui >> 1) & 1);
-        for (int ui = issued_v > kStages ? issued_v - kStages : 0; ui < issued_v; ++ui)
-          mbar_drain(&bars->v_full[ui & 1], (ui >> 1) & 1);
+        if (*abort_flag && issued_v > 0) mbar_drain(&bars->v_full, (issued_v - 1) & 1);
+      } else {
+        // Thread 0 also issues the unit's q TMA load (same stage as its K).
+        if (tl == 0) tma_prefetch_desc(&tmQ);
+        int issued_q = 0;
+        for (int ui = 0; ui < n_units; ++ui) {
+          const int s = ui & 1;
+          const long u = first + (long)ui * gridDim.x;
+          const uint32_t prev = ((ui >> 1) - 1) & 1;
+          if (ui >= kStages && !mbar_wait(&bars->qk_free[s], prev, abort_flag)) break;
+          if (tl == 0) {
+            mbar_arrive_expect_tx(&bars->q_full[s], L::kQBytes);
+            for (int cq = 0; cq < L::HC; ++cq)
+              tma_load_3d(smem + s * L::kQKStage + L::OFF_Q + cq * L::kQChunk, &tmQ, &bars->q_full[s], cq * 16, 0,
+                          (int)u);
+            issued_q = ui + 1;
+          }
+          if (c < kN / 4) {
+            uint8_t* dst = smem + s * L::kQKStage + L::OFF_K + dst0;
+            const T* src = kt + u * (long)HD * kN + 4 * c;
+#pragma unroll 8
+            for (int d = 0; d < HD; ++d) cp_async_8(dst + 16 * d, src + d * kN);
+          }
+          cp_async_wait_all();
+          fence_proxy_async_smem();
+          mbar_arrive(&bars->k_full[s]);
+        }
+        cp_async_wait_all();
+        if (tl == 0 && *abort_flag) {
+          // drain this CTA's own TMA copies still in flight before the CTA can exit
+          for (int ui = issued_q > kStages ? issued_q - kStages : 0; ui < issued_q; ++ui)
+            mbar_drain(&bars->q_full[ui & 1], (ui >> 1) & 1);
+        }
       }
     }
   } else {
@@ -463,16 +470,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->t_free[t]);  // O_t read and S_t columns free for the next unit's S MMA
-      if (live && rt < kN) {
-        uint4* orow = reinterpret_cast<uint4*>(out + (u * kN + rt) * HD);
+      // Rows -> this warp's 32-row block of the staging buffer (its previous bulk store has read it), then
+      // one bulk store of the block's real rows, which are contiguous in `out`.
+      const int nrows = kN - (128 * t + 32 * wq) < 32 ? kN - (128 * t + 32 * wq) : 32;
+      if (live) {
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+        uint8_t* stg_row = smem + L::OFF_STG + t * L::kStgTile + (32 * wq + lane) * (HD * 2);
+        if (lane < nrows) {
 #pragma unroll
-        for (int c0 = 0; c0 < HD / 16; ++c0) {
-          orow[2 * c0] = make_uint4(pw[c0][0], pw[c0][1], pw[c0][2], pw[c0][3]);
-          orow[2 * c0 + 1] = make_uint4(pw[c0][4], pw[c0][5], pw[c0][6], pw[c0][7]);
+          for (int c0 = 0; c0 < HD / 16; ++c0) {
+            reinterpret_cast<uint4*>(stg_row)[2 * c0] = make_uint4(pw[c0][0], pw[c0][1], pw[c0][2], pw[c0][3]);
+            reinterpret_cast<uint4*>(stg_row)[2 * c0 + 1] = make_uint4(pw[c0][4], pw[c0][5], pw[c0][6], pw[c0][7]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          bulk_store(out + (u * kN + 128 * t + 32 * wq) * HD, smem + L::OFF_STG + t * L::kStgTile + 32 * wq * (HD * 2),
+                     (uint32_t)(nrows * HD * 2));
+          bulk_commit();
         }
       }
     }
   }
+  if (warp >= 4 && lane == 0) bulk_wait();  // this warp's output stores have completed
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
