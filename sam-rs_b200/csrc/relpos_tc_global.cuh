@@ -370,11 +370,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
-            okk = mbar_wait(&bars->p_full[q], j & 1, abort_flag);
-            // the operands of this tile and of the next S: waited on before the MMA run, so that PV_q(j) and
-            // S_q(j+1) issue back to back
-            if (okk && q == 0) okk = mbar_wait(&bars->v_full[st], (j / kStages) & 1, abort_flag);
+            // the operands of this tile and of the next S (loaded long before; checked while the softmax
+            // still runs), then the softmax's P: PV_q(j) and S_q(j+1) issue back to back
+            if (q == 0) okk = mbar_wait(&bars->v_full[st], (j / kStages) & 1, abort_flag);
             if (okk && q == 0 && j + 1 < kNT) okk = mbar_wait(&bars->k_full[st1], ((j + 1) / kStages) & 1, abort_flag);
+            if (okk) okk = mbar_wait(&bars->p_full[q], j & 1, abort_flag);
             if (!okk) break;
             tc_fence_after();
 #pragma unroll
