@@ -385,34 +385,70 @@ def run_ours(args):
 
 def run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world):
     """Same workload through the C ABI with host (pinned) buffers: every layer copies its q, kt, v
-    host->device, runs the op, and copies its output device->host, all inside the timed region."""
+    host->device, runs the op, and copies its output device->host, all inside the timed region.
+    Serving-style pipelining: two device buffer sets per layer kind and three streams (upload, compute,
+    download) ordered by events, so layer l+1's upload, layer l's kernel and layer l-1's download overlap
+    (PCIe is full duplex)."""
     import torch
     host = {}
+    dev = {}
     for kind, s in sets.items():
         host[kind] = {k: torch.empty(s[k].shape, dtype=s[k].dtype, pin_memory=True) for k in ("q", "kt", "v", "out")}
         for k in ("q", "kt", "v"):
             host[kind][k].copy_(s[k])
+        dev[kind] = [s, {k: torch.empty_like(s[k]) for k in ("q", "kt", "v", "out")}]
     torch.cuda.synchronize()
+    s_up, s_down = torch.cuda.Stream(device), torch.cuda.Stream(device)
     sptr = stream.cuda_stream
     scale = HD ** -0.5
+    # per (kind, buffer): the compute that last read the inputs / wrote the output, the download of it
+    comp_done = {k: [None, None] for k in sets}
+    down_done = {k: [None, None] for k in sets}
     h2d = d2h = 0
 
     def step():
         nonlocal h2d, d2h
         h2d = d2h = 0
+        use = {k: 0 for k in sets}
         for li, (kind, h, w, bh) in enumerate(geoms):
-            s, hb = sets[kind], host[kind]
-            for k in ("q", "kt", "v"):
-                s[k].copy_(hb[k], non_blocking=True)
-                h2d += hb[k].numel() * hb[k].element_size()
-            rc = lib.samrs_relpos_attn_fwd(s["q"].data_ptr(), s["kt"].data_ptr(), s["v"].data_ptr(),
-                                           tables[li].data_ptr(), s["out"].data_ptr(), bh, h, w, HD, scale, 2, sptr)
+            bi = use[kind] & 1
+            use[kind] += 1
+            d, hb = dev[kind][bi], host[kind]
+            up = torch.cuda.Event()
+            with torch.cuda.stream(s_up):
+                if comp_done[kind][bi] is not None:
+                    s_up.wait_event(comp_done[kind][bi])  # the kernel that read this buffer set is done
+                for k in ("q", "kt", "v"):
+                    d[k].copy_(hb[k], non_blocking=True)
+                    h2d += hb[k].numel() * hb[k].element_size()
+                up.record(s_up)
+            stream.wait_event(up)
+            if down_done[kind][bi] is not None:
+                stream.wait_event(down_done[kind][bi])  # the previous output in this set is on the host
+            rc = lib.samrs_relpos_attn_fwd(d["q"].data_ptr(), d["kt"].data_ptr(), d["v"].data_ptr(),
+                                           tables[li].data_ptr(), d["out"].data_ptr(), bh, h, w, HD, scale, 2, sptr)
             if rc != 0:
                 raise RuntimeError(lib.samrs_last_error().decode())
-            hb["out"].copy_(s["out"], non_blocking=True)
-            d2h += hb["out"].numel() * hb["out"].element_size()
+            cd = torch.cuda.Event()
+            cd.record(stream)
+            comp_done[kind][bi] = cd
+            dd = torch.cuda.Event()
+            with torch.cuda.stream(s_down):
+                s_down.wait_event(cd)
+                hb["out"].copy_(d["out"], non_blocking=True)
+                d2h += hb["out"].numel() * hb["out"].element_size()
+                dd.record(s_down)
+            down_done[kind][bi] = dd
+
+    def join():
+        # the compute stream waits for the other two, so one event on it closes the step
+        for st in (s_up, s_down):
+            e = torch.cuda.Event()
+            e.record(st)
+            stream.wait_event(e)
 
     step()
+    join()
     torch.cuda.synchronize()
     k = max(1, min(args.steps, args.e2e_steps))
     if dist is not None:
@@ -421,14 +457,18 @@ def run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world):
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record(stream)
+    s_up.wait_event(a)
+    s_down.wait_event(a)
     for _ in range(k):
         step()
+    join()
     b.record(stream)
     torch.cuda.synchronize()
     ms = max_over_ranks(a.elapsed_time(b), dist, device)
     flops = sum(layer_flops(h, w, bh) for (_, h, w, bh) in geoms) * k * world
     return {"value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": k, "ms_per_step": ms / k, "path": "C ABI samrs_relpos_attn_fwd, pinned host buffers"}
+            "steps": k, "ms_per_step": ms / k,
+            "path": "C ABI samrs_relpos_attn_fwd, pinned host buffers, upload/compute/download streams"}
 
 
 def main(argv=None):
