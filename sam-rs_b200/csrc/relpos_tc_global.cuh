@@ -318,84 +318,86 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------------- MMA issuer
-      if (lane == 0) {
-        constexpr uint32_t idS = idesc_f16(kBf16, 128, 128, false, true);    // S = Q K^T, K MN-major
-        constexpr uint32_t idRW = idesc_f16(kBf16, 128, 128, false, false);  // RW = Q Tw^T
-        constexpr uint32_t idRH = idesc_f16(kBf16, 128, 80, false, false);   // RH = Q Th^T
-        constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);    // O += P V, V MN-major
-        const uint32_t sb = smem_u32(smem);
-        const uint64_t dQ = smem_desc(sb + L::OFF_Q, 16, 256, kLayoutSw32);
-        const uint64_t dTh = smem_desc(sb + L::OFF_TH, 16, 256, kLayoutSw32);
-        const uint64_t dTw = smem_desc(sb + L::OFF_TW, 16, 256, kLayoutSw32);
-        const uint64_t dK = smem_desc(sb + L::OFF_K, L::kKAtom, 1024, kLayoutSw128);
-        const uint64_t dV = smem_desc(sb + L::OFF_V, L::kChunkBytes, 256, kLayoutSw32);
-        // S_q from K stage st into the S_q columns
-        auto issue_s = [&](int q, int st) {
-          const uint64_t dKs = desc_add(dK, st * L::kKBytes);
+      // The whole warp runs the issue loop (waits, descriptors); lane 0, elected inside each MMA and commit,
+      // issues them.
+      constexpr uint32_t idS = idesc_f16(kBf16, 128, 128, false, true);    // S = Q K^T, K MN-major
+      constexpr uint32_t idRW = idesc_f16(kBf16, 128, 128, false, false);  // RW = Q Tw^T
+      constexpr uint32_t idRH = idesc_f16(kBf16, 128, 80, false, false);   // RH = Q Th^T
+      constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);    // O += P V, V MN-major
+      const uint32_t sb = smem_u32(smem);
+      const uint64_t dQ = smem_desc(sb + L::OFF_Q, 16, 256, kLayoutSw32);
+      const uint64_t dTh = smem_desc(sb + L::OFF_TH, 16, 256, kLayoutSw32);
+      const uint64_t dTw = smem_desc(sb + L::OFF_TW, 16, 256, kLayoutSw32);
+      const uint64_t dK = smem_desc(sb + L::OFF_K, L::kKAtom, 1024, kLayoutSw128);
+      const uint64_t dV = smem_desc(sb + L::OFF_V, L::kChunkBytes, 256, kLayoutSw32);
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+      };
+      // S_q from K stage st into the S_q columns
+      auto issue_s = [&](int q, int st) {
+        const uint64_t dKs = desc_add(dK, st * L::kKBytes);
+#pragma unroll
+        for (int c = 0; c < L::HC; ++c)
+          mma_ss_w(tmem + q * 128, desc_add(dQ, q * L::kQBytes + c * L::kChunkBytes), desc_add(dKs, c * 2048), idS,
+                   c > 0);
+      };
+      bool okk = wait(&bars->q_full, 0);
+      if (okk) {
+        tc_fence_after();
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
 #pragma unroll
           for (int c = 0; c < L::HC; ++c)
-            mma_ss(tmem + q * 128, desc_add(dQ, q * L::kQBytes + c * L::kChunkBytes), desc_add(dKs, c * 2048), idS,
-                   c > 0);
-        };
-        bool okk = mbar_wait(&bars->q_full, 0, abort_flag);
-        if (okk) {
-          tc_fence_after();
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-#pragma unroll
-            for (int c = 0; c < L::HC; ++c)
-              mma_ss(tmem + q * 128, desc_add(dQ, q * L::kQBytes + c * L::kChunkBytes),
+            mma_ss_w(tmem + q * 128, desc_add(dQ, q * L::kQBytes + c * L::kChunkBytes),
                      desc_add(dTw, c * L::kChunkBytes), idRW, c > 0);
 #pragma unroll
-            for (int c = 0; c < L::HC; ++c)
-              mma_ss(tmem + 256 + q * 80, desc_add(dQ, q * L::kQBytes + c * L::kChunkBytes),
+          for (int c = 0; c < L::HC; ++c)
+            mma_ss_w(tmem + 256 + q * 80, desc_add(dQ, q * L::kQBytes + c * L::kChunkBytes),
                      desc_add(dTh, c * L::kChunkBytes), idRH, c > 0);
-          }
-          mma_commit(&bars->pro_done);
-          // S_q overwrites RW_q and the rh park aliases the tables: both query tiles must be done with them
-          okk = mbar_wait(&bars->bias_done[0], 0, abort_flag) && mbar_wait(&bars->bias_done[1], 0, abort_flag) &&
-                mbar_wait(&bars->k_full[0], 0, abort_flag);
         }
-        if (okk) {
-          tc_fence_after();
-          issue_s(0, 0);
-          mma_commit(&bars->s_full[0]);
-          issue_s(1, 0);
-          mma_commit(&bars->s_full[1]);
-          mma_commit(&bars->k_empty[0]);
-        }
-        for (int j = 0; j < kNT && okk; ++j) {
-          const int st = j % kStages, st1 = (j + 1) % kStages;
-          const uint64_t dVs = desc_add(dV, st * L::kVBytes);
-          const uint32_t acc0 = j > 0 ? 1u : 0u;
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            // the operands of this tile and of the next S (loaded long before; checked while the softmax
-            // still runs), then the softmax's P: PV_q(j) and S_q(j+1) issue back to back
-            if (q == 0) okk = mbar_wait(&bars->v_full[st], (j / kStages) & 1, abort_flag);
-            if (okk && q == 0 && j + 1 < kNT) okk = mbar_wait(&bars->k_full[st1], ((j + 1) / kStages) & 1, abort_flag);
-            if (okk) okk = mbar_wait(&bars->p_full[q], j & 1, abort_flag);
-            if (!okk) break;
-            tc_fence_after();
-#pragma unroll
-            for (int s = 0; s < kBK / 16; ++s)
-              mma_ts(tmem + 256 + q * HD, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV, s > 0 ? 1u : acc0);
-            if (j + 1 < kNT) {
-              // issued after PV_q(j), which reads P_q(j) from the same columns: in-order execution
-              issue_s(q, st1);
-              mma_commit(&bars->s_full[q]);
-            } else {
-              mma_commit(&bars->o_done[q]);
-            }
-          }
-          if (!okk) break;
-          mma_commit(&bars->v_empty[st]);
-          if (j + 1 < kNT) mma_commit(&bars->k_empty[st1]);
-        }
-        // every MMA issued by this thread has completed before the CTA tears down TMEM
-        mma_commit(&bars->final_mma);
-        mbar_drain(&bars->final_mma, 0);
+        mma_commit_w(&bars->pro_done);
+        // S_q overwrites RW_q and the rh park aliases the tables: both query tiles must be done with them
+        okk = wait(&bars->bias_done[0], 0) && wait(&bars->bias_done[1], 0) && wait(&bars->k_full[0], 0);
       }
+      if (okk) {
+        tc_fence_after();
+        issue_s(0, 0);
+        mma_commit_w(&bars->s_full[0]);
+        issue_s(1, 0);
+        mma_commit_w(&bars->s_full[1]);
+        mma_commit_w(&bars->k_empty[0]);
+      }
+      for (int j = 0; j < kNT && okk; ++j) {
+        const int st = j % kStages, st1 = (j + 1) % kStages;
+        const uint64_t dVs = desc_add(dV, st * L::kVBytes);
+        const uint32_t acc0 = j > 0 ? 1u : 0u;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          // the operands of this tile and of the next S (loaded long before; checked while the softmax
+          // still runs), then the softmax's P: PV_q(j) and S_q(j+1) issue back to back
+          if (q == 0) okk = wait(&bars->v_full[st], (j / kStages) & 1);
+          if (okk && q == 0 && j + 1 < kNT) okk = wait(&bars->k_full[st1], ((j + 1) / kStages) & 1);
+          if (okk) okk = wait(&bars->p_full[q], j & 1);
+          if (!okk) break;
+          tc_fence_after();
+#pragma unroll
+          for (int s = 0; s < kBK / 16; ++s)
+            mma_ts_w(tmem + 256 + q * HD, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV, s > 0 ? 1u : acc0);
+          if (j + 1 < kNT) {
+            // issued after PV_q(j), which reads P_q(j) from the same columns: in-order execution
+            issue_s(q, st1);
+            mma_commit_w(&bars->s_full[q]);
+          } else {
+            mma_commit_w(&bars->o_done[q]);
+          }
+        }
+        if (!okk) break;
+        mma_commit_w(&bars->v_empty[st]);
+        if (j + 1 < kNT) mma_commit_w(&bars->k_empty[st1]);
+      }
+      // every MMA issued by this warp has completed before the CTA tears down TMEM
+      mma_commit_w(&bars->final_mma);
+      mbar_drain(&bars->final_mma, 0);
     }
   } else {
     regs_inc<kRegsHigh>();

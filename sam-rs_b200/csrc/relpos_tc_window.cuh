@@ -23,7 +23,7 @@
 // tiles' PV MMAs completed; the load has the next unit's softmax to land). Output rows are staged in
 // shared memory and written back by one bulk store per warp.
 //
-// Warps: 0 / 1 MMA issuers of query tile 1 / 0 (one thread each, so the two tiles' S -> softmax -> PV ->
+// Warps: 0 / 1 MMA issuers of query tile 1 / 0 (one warp each, so the two tiles' S -> softmax -> PV ->
 // epilogue chains never wait on each other), 2-3 kt loaders (thread 0 also issues the q TMA loads, the
 // last thread the v TMA loads; warp 2 allocates TMEM), 4-7 / 8-11 softmax + epilogue of query tile 0 / 1 (thread = query
 // row = TMEM lane); warp 11 covers rows 224..255 only, which are all padding, so it only keeps the
@@ -321,42 +321,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     regs_dec<kRegsLow>();
     if (warp < 2) {
       // ---------------------------------------------------------------- MMA issuer of tile t
-      if (lane == 0) {
-        const int t = 1 - warp;
-        constexpr uint32_t idS = idesc_f16(kBf16, 128, kNB, false, true);
-        constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);
-        const uint32_t sb = smem_u32(smem);
-        const uint64_t dQ = smem_desc(sb + L::OFF_Q + t * 128 * 32, 16, 256, kLayoutSw32);
-        const uint64_t dK = smem_desc(sb + L::OFF_K, 128, L::kKSbo, kLayoutNone);
-        const uint64_t dV = smem_desc(sb + L::OFF_V, L::kVChunk, 256, kLayoutSw32);
-        const uint32_t tT = tmem + 256 * t;
-        bool okk = true;
-        for (int ui = 0; ui < n_units && okk; ++ui) {
-          const int s = ui & 1;
-          const uint32_t ph = (ui >> 1) & 1;
-          // S_t(u) overwrites the tile's columns: the softmax warps must have read O_t(u-1)
-          okk = mbar_wait(&bars->q_full[s], ph, abort_flag) && mbar_wait(&bars->k_full[s], ph, abort_flag) &&
-                (ui == 0 || mbar_wait(&bars->t_free[t], (ui - 1) & 1, abort_flag));
-          if (!okk) break;
-          tc_fence_after();
+      // The whole warp runs the issue loop; lane 0, elected inside each MMA and commit, issues them.
+      const int t = 1 - warp;
+      constexpr uint32_t idS = idesc_f16(kBf16, 128, kNB, false, true);
+      constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);
+      const uint32_t sb = smem_u32(smem);
+      const uint64_t dQ = smem_desc(sb + L::OFF_Q + t * 128 * 32, 16, 256, kLayoutSw32);
+      const uint64_t dK = smem_desc(sb + L::OFF_K, 128, L::kKSbo, kLayoutNone);
+      const uint64_t dV = smem_desc(sb + L::OFF_V, L::kVChunk, 256, kLayoutSw32);
+      const uint32_t tT = tmem + 256 * t;
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+      };
+      bool okk = true;
+      for (int ui = 0; ui < n_units && okk; ++ui) {
+        const int s = ui & 1;
+        const uint32_t ph = (ui >> 1) & 1;
+        // S_t(u) overwrites the tile's columns: the softmax warps must have read O_t(u-1)
+        okk = wait(&bars->q_full[s], ph) && wait(&bars->k_full[s], ph) &&
+              (ui == 0 || wait(&bars->t_free[t], (ui - 1) & 1));
+        if (!okk) break;
+        tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < L::HC; ++c)
-            mma_ss(tT, desc_add(dQ, s * L::kQKStage + c * L::kQChunk), desc_add(dK, s * L::kQKStage + c * 256), idS,
+        for (int c = 0; c < L::HC; ++c)
+          mma_ss_w(tT, desc_add(dQ, s * L::kQKStage + c * L::kQChunk), desc_add(dK, s * L::kQKStage + c * 256), idS,
                    c > 0);
-          mma_commit(&bars->s_full[t]);
-          mma_commit(&bars->qk_free[s]);  // this tile's reads of the unit's Q and K are done once S_t completes
-          okk = mbar_wait(&bars->v_full, ui & 1, abort_flag) && mbar_wait(&bars->p_full[t], ui & 1, abort_flag);
-          if (!okk) break;
-          tc_fence_after();
+        mma_commit_w(&bars->s_full[t]);
+        mma_commit_w(&bars->qk_free[s]);  // this tile's reads of the unit's Q and K are done once S_t completes
+        okk = wait(&bars->v_full, ui & 1) && wait(&bars->p_full[t], ui & 1);
+        if (!okk) break;
+        tc_fence_after();
 #pragma unroll
-          for (int k = 0; k < kNP / 16; ++k)
-            mma_ts(tT + 128, tT + 8 * k, desc_add(dV, k * 512), idPV, k > 0 ? 1u : 0u);
-          mma_commit(&bars->o_full[t]);
-          mma_commit(&bars->v_free);
-        }
-        mma_commit(&bars->final_mma[t]);
-        mbar_drain(&bars->final_mma[t], 0);
+        for (int k = 0; k < kNP / 16; ++k)
+          mma_ts_w(tT + 128, tT + 8 * k, desc_add(dV, k * 512), idPV, k > 0 ? 1u : 0u);
+        mma_commit_w(&bars->o_full[t]);
+        mma_commit_w(&bars->v_free);
       }
+      mma_commit_w(&bars->final_mma[t]);
+      mbar_drain(&bars->final_mma[t], 0);
     } else {
       // ---------------------------------------------------------------- kt loaders (cp.async relayout)
       const int tl = threadIdx.x - 64;

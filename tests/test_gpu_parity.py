@@ -120,6 +120,34 @@ def test_vith_full_batch_properties(samrs, cuda, h, w, bh, hd):
         assert err < HALF_TOL, (b, err)
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("hd", [64, 80])
+def test_global_late_max_jumps(samrs, cuda, hd, dt):
+    """Row maxima that jump late in the key sequence (64x64 global layer): the online softmax's rescaling.
+
+    Every query has a large first coordinate and a few keys have a large first coordinate, so that a
+    query's max logit jumps by 25 to 30 log2 units at a later 128-key tile (far beyond the largest P a
+    16-bit type holds against the earlier reference): in the first tiles, in the middle, and in the last
+    tile only, per head. Most rows end up dominated by one key; in bf16 the dominant P carries its 8-bit
+    rounding (up to 2^-9 relative) into the output, so the bf16 bar here is 2^-8 instead of 3e-3."""
+    h = w = 64
+    q, kt, v, t = make_inputs(h, w, 3, hd, seed=hd + 5, table_std=0.5)
+    q[:, :, 0] = 4.0
+    jumps = {0: {128 * 1 + 3: 40.0, 128 * 9 + 77: 80.0, 128 * 31 + 127: 120.0},
+             1: {128 * 31 + 5: 80.0},
+             2: {128 * 2 + 64: 40.0, 128 * 3 + 1: 80.0, 128 * 4 + 2: 120.0, 128 * 20 + 90: 160.0}}
+    for b, keys in jumps.items():
+        for key, big in keys.items():
+            kt[b, 0, key] = big
+    scale = hd ** -0.5
+    qd, ktd, vd, td = (to_dev(x, dt, cuda) for x in (q, kt, v, t))
+    out = samrs.attention_relpos(qd, ktd, vd, td, h, w, scale)
+    assert samrs.device_status() == 0
+    ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, w, scale)
+    err = parity_err(out.float().cpu().numpy(), ref, dt)
+    assert err < (HALF_TOL if dt == "f16" else 2.0 ** -8), err
+
+
 def test_tc_and_simt_agree_bf16(samrs, cuda):
     for (h, w, bh, hd) in [(64, 64, 2, 80), (14, 14, 40, 80)]:
         q, kt, v, t = make_inputs(h, w, bh, hd, seed=99)
