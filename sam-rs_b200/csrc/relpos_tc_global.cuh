@@ -48,7 +48,7 @@ constexpr int kLaunchRegs = 96;  // 65536 / 640 rounded down to the allocation g
 // take 104: 128 x 64 + 512 x 104 = 61440 = 640 x 96.
 constexpr uint32_t kRegsLow = 64, kRegsHigh = 104;
 static_assert(128 * kRegsLow + 512 * kRegsHigh <= kThreads * kLaunchRegs, "register split exceeds the launch allotment");
-constexpr int kBQ = 128, kBK = 128, kSide = 64, kN = 4096, kNT = kN / kBK, kStages = 3;
+constexpr int kBQ = 128, kBK = 128, kSide = 64, kN = 4096, kNT = kN / kBK, kStages = 2;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
@@ -59,12 +59,16 @@ struct Layout {
   static constexpr int kQBytes = HC * kChunkBytes;    // a 128-row tile of q / v / table
   static constexpr int kKAtom = HD * 128;             // one [HD rows x 64 keys] SW128 box
   static constexpr int kKBytes = 2 * kKAtom;
-  static constexpr int kVBytes = kQBytes;
+  static constexpr int kVBytes = kQBytes;             // bytes of v loaded per stage
+  // A V stage holds the HC chunks of v and then a chunk of ones: the P.V MMA runs with N = HD + 16, so
+  // that O's last 16 columns accumulate the row sums of the 16-bit P exactly as the product uses them.
+  static constexpr int kVStage = (HC + 1) * kChunkBytes;
+  static constexpr int kOCols = HD + 16;
   static constexpr int kRhBytes = 64 * 256 * 4;       // rh park: [kh][256 rows] f32
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * kQBytes;
   static constexpr int OFF_V = OFF_K + kStages * kKBytes;
-  static constexpr int OFF_RH = OFF_V + kStages * kVBytes;
+  static constexpr int OFF_RH = OFF_V + kStages * kVStage;
   static constexpr int OFF_TH = OFF_RH;               // prologue only (aliases the rh park)
   static constexpr int OFF_TW = OFF_RH + kQBytes;
   static constexpr int OFF_BAR = OFF_RH + kRhBytes;
@@ -188,13 +192,12 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&v)[8], float2 c2, con
   }
 }
 
-// Pass 2: p = 2^(S*c + rw + (rh - m)) for both rows, pair sums, and the 16-bit pairs in the 16x128b store
-// order (pw[2i] row A, pw[2i+1] row B: P column 4(G0+i) + c = keys 8(G0+i) + 2c, +1). Staged (exponents,
-// then the ex2, then sums and packing) so the ex2 issue back to back.
+// Pass 2: p = 2^(S*c + rw + (rh - m)) for both rows as 16-bit pairs in the 16x128b store order (pw[2i]
+// row A, pw[2i+1] row B: P column 4(G0+i) + c = keys 8(G0+i) + 2c, +1). Staged (exponents, then the ex2,
+// then packing) so the ex2 issue back to back. The row sums come from the P.V MMA (ones block of V).
 template <int G0, bool BF16>
 __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, const float2 (&rwA)[8],
-                                          const float2 (&rwB)[8], float2 bA, float2 bB, float2& sA, float2& sB,
-                                          uint32_t (&pw)[4]) {
+                                          const float2 (&rwB)[8], float2 bA, float2 bB, uint32_t (&pw)[4]) {
   float x[8];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
@@ -218,8 +221,6 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, con
   }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    sA = sm100::add2(sA, make_float2(x[4 * i], x[4 * i + 1]));
-    sB = sm100::add2(sB, make_float2(x[4 * i + 2], x[4 * i + 3]));
     pw[2 * i] = sm100::pack2(x[4 * i], x[4 * i + 1], BF16);
     pw[2 * i + 1] = sm100::pack2(x[4 * i + 2], x[4 * i + 3], BF16);
   }
@@ -269,6 +270,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
   }
+  {
+    // the ones block of every V stage (the TMA loads never write it); read by the MMA (async proxy)
+    const uint32_t one2 = kBf16 ? 0x3F803F80u : 0x3C003C00u;
+    for (int idx = threadIdx.x; idx < kStages * L::kChunkBytes / 16; idx += kThreads) {
+      const int st = idx / (L::kChunkBytes / 16), o = idx % (L::kChunkBytes / 16);
+      reinterpret_cast<uint4*>(smem + L::OFF_V + st * L::kVStage + L::HC * L::kChunkBytes)[o] =
+          make_uint4(one2, one2, one2, one2);
+    }
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -304,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j >= kStages && !mbar_wait(&bars->v_empty[st], prev, abort_flag)) break;
           mbar_arrive_expect_tx(&bars->v_full[st], L::kVBytes);
           for (int c = 0; c < L::HC; ++c)
-            tma_load_2d(smem + L::OFF_V + st * L::kVBytes + c * L::kChunkBytes, &tmV, &bars->v_full[st], c * 16,
+            tma_load_2d(smem + L::OFF_V + st * L::kVStage + c * L::kChunkBytes, &tmV, &bars->v_full[st], c * 16,
                         (int)(bh * kN + j * kBK));
           issued_v = j + 1;
         }
@@ -323,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idS = idesc_f16(kBf16, 128, 128, false, true);    // S = Q K^T, K MN-major
       constexpr uint32_t idRW = idesc_f16(kBf16, 128, 128, false, false);  // RW = Q Tw^T
       constexpr uint32_t idRH = idesc_f16(kBf16, 128, 80, false, false);   // RH = Q Th^T
-      constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);    // O += P V, V MN-major
+      constexpr uint32_t idPV = idesc_f16(kBf16, 128, L::kOCols, false, true);  // O += P [V | 1], MN-major
       const uint32_t sb = smem_u32(smem);
       const uint64_t dQ = smem_desc(sb + L::OFF_Q, 16, 256, kLayoutSw32);
       const uint64_t dTh = smem_desc(sb + L::OFF_TH, 16, 256, kLayoutSw32);
@@ -369,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int j = 0; j < kNT && okk; ++j) {
         const int st = j % kStages, st1 = (j + 1) % kStages;
-        const uint64_t dVs = desc_add(dV, st * L::kVBytes);
+        const uint64_t dVs = desc_add(dV, st * L::kVStage);
         const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
@@ -382,7 +393,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
 #pragma unroll
           for (int s = 0; s < kBK / 16; ++s)
-            mma_ts_w(tmem + 256 + q * HD, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV, s > 0 ? 1u : acc0);
+            mma_ts_w(tmem + 256 + q * L::kOCols, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV,
+                     s > 0 ? 1u : acc0);
           if (j + 1 < kNT) {
             // issued after PV_q(j), which reads P_q(j) from the same columns: in-order execution
             issue_s(q, st1);
@@ -411,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rA = lb + (lane >> 2);      // this thread's rows rA and rA + 8 within the tile
     const int prowA = q * 128 + rA, prowB = prowA + 8;
     const uint32_t tS = tmem + ((uint32_t)lb << 16) + q * 128;
-    const uint32_t tO = tmem + ((uint32_t)lb << 16) + 256 + q * HD;
+    const uint32_t tO = tmem + ((uint32_t)lb << 16) + 256 + q * L::kOCols;
     const float c_log2 = scale * kLog2e;
     const float2 c2 = make_float2(c_log2, c_log2);
     float2 rwA[8], rwB[8];
@@ -460,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->bias_done[q]);
     }
-    float mrA = -INFINITY, mrB = -INFINITY, lA = 0.f, lB = 0.f;
+    float mrA = -INFINITY, mrB = -INFINITY;
     for (int j = 0; j < kNT && okk; ++j) {
       okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
       if (!okk) break;
@@ -503,7 +515,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // pass 2: p = 2^(S*c + rw + rh - m); P of chunk k (16-bit pairs, columns 8k..8k+7) lands on scores of
       // chunk k/2 <= k, already read. The load of chunk k+1 is in flight meanwhile.
-      float2 sA = make_float2(0.f, 0.f), sB = make_float2(0.f, 0.f);
       {
         const float2 bA0 = make_float2(rhA0 - mrA, rhA0 - mrA), bA1 = make_float2(rhA1 - mrA, rhA1 - mrA);
         const float2 bB0 = make_float2(rhB0 - mrB, rhB0 - mrB), bB1 = make_float2(rhB1 - mrB, rhB1 - mrB);
@@ -516,19 +527,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t(&nxt)[8] = (k & 1) ? v0 : v1;
           if constexpr (k + 1 < 8) tmem_ld_16x256b_x2(tS + 16 * (k + 1), nxt);
           if constexpr (k < 4)
-            chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA0, bB0, sA, sB, pw);
+            chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA0, bB0, pw);
           else
-            chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA1, bB1, sA, sB, pw);
+            chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA1, bB1, pw);
           tmem_st_16x128b_x2(tS + 8 * k, pw);
           if constexpr (k + 1 < 8) tmem_wait_ld_regs(nxt);
         });
       }
-      lA = lA * alA + (sA.x + sA.y);  // this thread's share of the row sum (combined in the epilogue)
-      lB = lB * alB + (sB.x + sB.y);
-      // O rescale: PV_q(j-1) has completed (it was issued before S_q(j), whose commit we waited on).
+      // O and row-sum rescale: PV_q(j-1) has completed (it was issued before S_q(j), whose commit we waited
+      // on).
       if (__any_sync(0xffffffffu, (needA || needB) && j > 0)) {
 #pragma unroll
-        for (int c0 = 0; c0 < HD; c0 += 16) {
+        for (int c0 = 0; c0 < L::kOCols; c0 += 16) {
           uint32_t ov[8];
           tmem_ld_16x256b_x2(tO + c0, ov);
           tmem_wait_ld_regs(ov);
@@ -552,11 +562,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (okk) okk = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[q], 0, abort_flag));
     if (okk) {
       tc_fence_after();
-      lA += __shfl_xor_sync(0xffffffffu, lA, 1);
-      lB += __shfl_xor_sync(0xffffffffu, lB, 1);
-      lA += __shfl_xor_sync(0xffffffffu, lA, 2);
-      lB += __shfl_xor_sync(0xffffffffu, lB, 2);
-      const float invA = 1.f / lA, invB = 1.f / lB;
+      // every column of the ones block holds the row sum
+      uint32_t lv[8];
+      tmem_ld_16x256b_x2(tO + HD, lv);
+      tmem_wait_ld_regs(lv);
+      const float invA = 1.f / __uint_as_float(lv[0]), invB = 1.f / __uint_as_float(lv[2]);
       T* oA = out + (bh * kN + row0 + prowA) * HD + 2 * c;
       T* oB = oA + 8 * HD;
 #pragma unroll

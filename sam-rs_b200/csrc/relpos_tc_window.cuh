@@ -172,10 +172,10 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&sv)[32], float2 c2, c
   }
 }
 
-// Row max over the 196 keys: loads two chunks per wait.
+// Row max over the 196 keys: two chunks per wait, the next two loads in flight while a pair is reduced.
 __device__ __forceinline__ float row_max(uint32_t tS, float2 c2, const Bias& b) {
   using namespace sm100;
-  uint32_t a[32], bb[32];
+  uint32_t a[32], bb[32], a2[32], bb2[32];
   float m[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) m[i] = -INFINITY;
@@ -183,23 +183,23 @@ __device__ __forceinline__ float row_max(uint32_t tS, float2 c2, const Bias& b) 
   tmem_ld32(tS + 32, bb);
   tmem_wait_ld_regs(a);
   tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 64, a2);
+  tmem_ld32(tS + 96, bb2);
   chunk_max<0>(a, c2, b, m);
   chunk_max<1>(bb, c2, b, m);
-  tmem_ld32(tS + 64, a);
-  tmem_ld32(tS + 96, bb);
-  tmem_wait_ld_regs(a);
-  tmem_wait_ld_regs(bb);
-  chunk_max<2>(a, c2, b, m);
-  chunk_max<3>(bb, c2, b, m);
+  tmem_wait_ld_regs(a2);
+  tmem_wait_ld_regs(bb2);
   tmem_ld32(tS + 128, a);
   tmem_ld32(tS + 160, bb);
+  chunk_max<2>(a2, c2, b, m);
+  chunk_max<3>(bb2, c2, b, m);
   tmem_wait_ld_regs(a);
   tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 192, a2);  // columns 192..223: keys 192..195
   chunk_max<4>(a, c2, b, m);
   chunk_max<5>(bb, c2, b, m);
-  tmem_ld32(tS + 192, a);  // columns 192..223: keys 192..195
-  tmem_wait_ld_regs(a);
-  chunk_max<6>(a, c2, b, m);
+  tmem_wait_ld_regs(a2);
+  chunk_max<6>(a2, c2, b, m);
   return max3(max3(m[0], m[1], m[2]), max3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 
@@ -459,15 +459,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t pw[HD / 16][8];
       if (live) {
         const float inv = 1.f / sum;
+        uint32_t ov[HD / 16][16];
 #pragma unroll
-        for (int c0 = 0; c0 < HD / 16; ++c0) {
-          uint32_t ov[16];
-          tmem_ld16(tO + 16 * c0, ov);
-          tmem_wait_ld_regs(ov);
+        for (int c0 = 0; c0 < HD / 16; ++c0) tmem_ld16(tO + 16 * c0, ov[c0]);
+#pragma unroll
+        for (int c0 = 0; c0 < HD / 16; ++c0) tmem_wait_ld_regs(ov[c0]);
+#pragma unroll
+        for (int c0 = 0; c0 < HD / 16; ++c0)
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            pw[c0][e] = pack2(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv, kBf16);
-        }
+            pw[c0][e] = pack2(__uint_as_float(ov[c0][2 * e]) * inv, __uint_as_float(ov[c0][2 * e + 1]) * inv, kBf16);
       }
       tc_fence_before();
       __syncwarp();
