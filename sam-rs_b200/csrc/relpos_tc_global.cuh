@@ -51,6 +51,10 @@ static_assert(128 * kRegsLow + 512 * kRegsHigh <= kThreads * kLaunchRegs, "regis
 constexpr int kBQ = 128, kBK = 128, kSide = 64, kN = 4096, kNT = kN / kBK, kStages = 2;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
+// bf16: speculative single-pass tiles (see the softmax). The predicted max is capped kSpecCap above the
+// row's running max, the reference is raised once the prediction passes it by kSpecRaise, and a CTA whose
+// tiles saw an exponent above kSpecLimit (P > 2^64) or a non-finite output is recomputed exactly.
+constexpr float kSpecCap = 64.f, kSpecRaise = 4.f, kSpecLimit = 64.f;
 
 template <int HD>
 struct Layout {
@@ -83,8 +87,10 @@ struct Bars {
   uint64_t q_full, pro_done, final_mma;
   uint64_t k_full[kStages], v_full[kStages], k_empty[kStages], v_empty[kStages];
   uint64_t bias_done[2], s_full[2], p_full[2], o_done[2];
+  uint64_t pass_sync;  // bf16: end of the speculative pass (producer, issuer and the 16 softmax warps)
   uint32_t tmem_base;
   int abort_flag;
+  int rerun;  // bf16: a softmax thread asks for the exact pass
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
 
@@ -195,9 +201,11 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&v)[8], float2 c2, con
 // Pass 2: p = 2^(S*c + rw + (rh - m)) for both rows as 16-bit pairs in the 16x128b store order (pw[2i]
 // row A, pw[2i+1] row B: P column 4(G0+i) + c = keys 8(G0+i) + 2c, +1). Staged (exponents, then the ex2,
 // then packing) so the ex2 issue back to back. The row sums come from the P.V MMA (ones block of V).
-template <int G0, bool BF16>
+// TRACK: also the largest exponent per row (xmA, xmB).
+template <int G0, bool BF16, bool TRACK>
 __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, const float2 (&rwA)[8],
-                                          const float2 (&rwB)[8], float2 bA, float2 bB, uint32_t (&pw)[4]) {
+                                          const float2 (&rwB)[8], float2 bA, float2 bB, uint32_t (&pw)[4],
+                                          float& xmA, float& xmB) {
   float x[8];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
@@ -210,6 +218,10 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, con
     x[4 * i + 1] = xa.y;
     x[4 * i + 2] = xb.x;
     x[4 * i + 3] = xb.y;
+  }
+  if constexpr (TRACK) {  // x[0,1,4,5] row A, x[2,3,6,7] row B
+    xmA = sm100::max3(xmA, sm100::max3(x[0], x[1], x[4]), x[5]);
+    xmB = sm100::max3(xmB, sm100::max3(x[2], x[3], x[6]), x[7]);
   }
   // 6 of the 8 exponentials on the exp unit, the row-B pair of the second block on the FMA pipe
 #pragma unroll
@@ -224,6 +236,185 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, con
     pw[2 * i] = sm100::pack2(x[4 * i], x[4 * i + 1], BF16);
     pw[2 * i + 1] = sm100::pack2(x[4 * i + 2], x[4 * i + 3], BF16);
   }
+}
+
+// State of one softmax thread: its two rows (A, B) of query tile q, their rw registers and the running
+// reference maxima. The tile steps are inline; the exact pass of a rerun is a separate function that gets
+// the state by value, so that the speculative loop keeps its registers.
+template <typename T, int HD>
+struct SoftmaxRows {
+  static constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  using L = Layout<HD>;
+  uint32_t tS, tO;         // this warp's S/P and O columns (lane base included)
+  float2 c2;               // scale * log2(e), twice
+  float2 rwA[8], rwB[8];   // rw of rows A and B for this thread's key pairs (log2 units)
+  const float* rh_park;    // rh per (key row, tile row)
+  int prowA, prowB;        // the rows within the CTA's 256
+  Bars* bars;
+  int q, lane;
+  T* oA;                   // output row A at this thread's column pair; row B is 8 rows further
+  volatile int* abort_flag;
+  float mrA, mrB;          // reference maxima
+
+  __device__ __forceinline__ float rh(int kh, int prow) const { return rh_park[kh * 256 + prow]; }
+
+  // Pass 2 over the tile with reference maxima (mrA, mrB): p = 2^(S*c + rw + rh - m); P of chunk k (16-bit
+  // pairs, columns 8k..8k+7) lands on scores of chunk k/2 <= k, already read. The load of chunk k+1 is in
+  // flight meanwhile. TRACK: the largest exponent per (row, 64-key half) into xm (A0, A1, B0, B1).
+  template <bool TRACK>
+  __device__ __forceinline__ void pass2(float rhA0, float rhA1, float rhB0, float rhB1, float (&xm)[4]) {
+    using namespace sm100;
+    const float2 bA0 = make_float2(rhA0 - mrA, rhA0 - mrA), bA1 = make_float2(rhA1 - mrA, rhA1 - mrA);
+    const float2 bB0 = make_float2(rhB0 - mrB, rhB0 - mrB), bB1 = make_float2(rhB1 - mrB, rhB1 - mrB);
+    uint32_t v0[8], v1[8], pw[4];
+    tmem_ld_16x256b_x2(tS + 0, v0);
+    tmem_wait_ld_regs(v0);
+    static_for<0, 8>([&](auto kk) {
+      constexpr int k = decltype(kk)::value;  // chunk k = blocks 2k, 2k+1
+      uint32_t(&cur)[8] = (k & 1) ? v1 : v0;
+      uint32_t(&nxt)[8] = (k & 1) ? v0 : v1;
+      if constexpr (k + 1 < 8) tmem_ld_16x256b_x2(tS + 16 * (k + 1), nxt);
+      if constexpr (k < 4)
+        chunk_exp<2 * k, kBf16, TRACK>(cur, c2, rwA, rwB, bA0, bB0, pw, xm[0], xm[2]);
+      else
+        chunk_exp<2 * k, kBf16, TRACK>(cur, c2, rwA, rwB, bA1, bB1, pw, xm[1], xm[3]);
+      tmem_st_16x128b_x2(tS + 8 * k, pw);
+      if constexpr (k + 1 < 8) tmem_wait_ld_regs(nxt);
+    });
+  }
+
+  // Exact tile: pass 1 gives the row maxima t of S*c + rw + rh (rh per 64-key half) across the row's four
+  // threads (BASE: also those of S*c + rw), the reference is raised if needed, then pass 2.
+  template <bool BASE>
+  __device__ __forceinline__ void exact_tile(int j, float rhA0, float rhA1, float rhB0, float rhB1, float& alA,
+                                             float& alB, bool& needA, bool& needB, float& tA, float& tB,
+                                             float& bA, float& bB) {
+    using namespace sm100;
+    {
+      uint32_t v0[8], v1[8];
+      float mA[2] = {-INFINITY, -INFINITY}, mB[2] = {-INFINITY, -INFINITY};
+      static_for<0, 4>([&](auto kk) {
+        constexpr int k = decltype(kk)::value;  // chunks 2k and 2k+1 = blocks 4k .. 4k+3
+        tmem_ld_16x256b_x2(tS + 32 * k, v0);
+        tmem_ld_16x256b_x2(tS + 32 * k + 16, v1);
+        tmem_wait_ld_regs(v0);
+        tmem_wait_ld_regs(v1);
+        chunk_max<4 * k>(v0, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
+        chunk_max<4 * k + 2>(v1, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
+      });
+      tA = fmaxf(mA[0] + rhA0, mA[1] + rhA1);
+      tB = fmaxf(mB[0] + rhB0, mB[1] + rhB1);
+      tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 1));
+      tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 1));
+      tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 2));
+      tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 2));
+      if constexpr (BASE) {
+        bA = fmaxf(mA[0], mA[1]);
+        bB = fmaxf(mB[0], mB[1]);
+        bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 1));
+        bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 1));
+        bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 2));
+        bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 2));
+      }
+    }
+    needA = (j == 0) || (tA > mrA + kRescaleThreshold);
+    needB = (j == 0) || (tB > mrB + kRescaleThreshold);
+    if (needA) {
+      const float mn = fmaxf(mrA, tA);
+      alA = ex2(mrA - mn);
+      mrA = mn;
+    }
+    if (needB) {
+      const float mn = fmaxf(mrB, tB);
+      alB = ex2(mrB - mn);
+      mrB = mn;
+    }
+    float xm[4];
+    pass2<false>(rhA0, rhA1, rhB0, rhB1, xm);
+  }
+
+  // End of a tile: O and row-sum rescale (PV_q(j-1) has completed: it was issued before S_q(j), whose
+  // commit was waited on), then one P-ready arrival per warp once every lane's P and O stores are done.
+  __device__ __forceinline__ void finish_tile(int j, bool needA, bool needB, float alA, float alB) {
+    using namespace sm100;
+    if (__any_sync(0xffffffffu, (needA || needB) && j > 0)) {
+#pragma unroll
+      for (int c0 = 0; c0 < L::kOCols; c0 += 16) {
+        uint32_t ov[8];
+        tmem_ld_16x256b_x2(tO + c0, ov);
+        tmem_wait_ld_regs(ov);
+        ov[0] = __float_as_uint(__uint_as_float(ov[0]) * alA);
+        ov[1] = __float_as_uint(__uint_as_float(ov[1]) * alA);
+        ov[4] = __float_as_uint(__uint_as_float(ov[4]) * alA);
+        ov[5] = __float_as_uint(__uint_as_float(ov[5]) * alA);
+        ov[2] = __float_as_uint(__uint_as_float(ov[2]) * alB);
+        ov[3] = __float_as_uint(__uint_as_float(ov[3]) * alB);
+        ov[6] = __float_as_uint(__uint_as_float(ov[6]) * alB);
+        ov[7] = __float_as_uint(__uint_as_float(ov[7]) * alB);
+        tmem_st_16x256b_x2(tO + c0, ov);
+      }
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->p_full[q]);
+  }
+
+  // Epilogue of a pass: O / l -> out once PV_q of the last tile has completed (l = any column of the ones
+  // block). Returns false if the pass was aborted; `finite` is cleared if an output is inf or NaN.
+  __device__ __forceinline__ bool epilogue(int pass, bool& finite) {
+    using namespace sm100;
+    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[q], pass & 1, abort_flag))) return false;
+    tc_fence_after();
+    uint32_t lv[8];
+    tmem_ld_16x256b_x2(tO + HD, lv);
+    tmem_wait_ld_regs(lv);
+    const float invA = 1.f / __uint_as_float(lv[0]), invB = 1.f / __uint_as_float(lv[2]);
+    T* oB = oA + 8 * HD;
+#pragma unroll
+    for (int c0 = 0; c0 < HD; c0 += 16) {
+      uint32_t ov[8];
+      tmem_ld_16x256b_x2(tO + c0, ov);
+      tmem_wait_ld_regs(ov);
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        y[e] = __uint_as_float(ov[e]) * ((e & 2) ? invB : invA);
+        finite &= fabsf(y[e]) < INFINITY;  // false for inf and NaN
+      }
+      *reinterpret_cast<uint32_t*>(oA + c0) = pack2(y[0], y[1], kBf16);
+      *reinterpret_cast<uint32_t*>(oA + c0 + 8) = pack2(y[4], y[5], kBf16);
+      *reinterpret_cast<uint32_t*>(oB + c0) = pack2(y[2], y[3], kBf16);
+      *reinterpret_cast<uint32_t*>(oB + c0 + 8) = pack2(y[6], y[7], kBf16);
+    }
+    return true;
+  }
+
+  // The exact pass over all key tiles, then the epilogue. kNT is even, so the S-ready and P-ready parities
+  // of tile j are the same in both passes. Returns false if it was aborted.
+  __device__ __forceinline__ bool exact_pass(int pass) {
+    using namespace sm100;
+    mrA = -INFINITY;
+    mrB = -INFINITY;
+    for (int j = 0; j < kNT; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag))) return false;
+      tc_fence_after();
+      bool needA, needB;
+      float alA = 1.f, alB = 1.f, tA, tB, bA, bB;
+      exact_tile<false>(j, rh(2 * j, prowA), rh(2 * j + 1, prowA), rh(2 * j, prowB), rh(2 * j + 1, prowB), alA,
+                        alB, needA, needB, tA, tB, bA, bB);
+      finish_tile(j, needA, needB, alA, alB);
+    }
+    bool finite = true;
+    return epilogue(pass, finite);
+  }
+};
+
+// The exact pass of a bf16 CTA whose speculative pass asked for it (rare): out of line, on a copy of the
+// state.
+template <typename T, int HD>
+__device__ __noinline__ bool softmax_rerun(SoftmaxRows<T, HD> rows) {
+  return rows.exact_pass(1);
 }
 
 template <typename T, int HD>
@@ -263,7 +454,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->p_full[q], 8);
       mbar_init(&bars->o_done[q], 1);
     }
+    mbar_init(&bars->pass_sync, 18);
     bars->abort_flag = 0;
+    bars->rerun = 0;
     fence_mbar_init();
   }
   if (warp == 2) {
@@ -284,6 +477,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // bf16 runs the speculative pass first and, for a CTA that asks for it, the exact pass; f16 runs the
+  // exact pass only (its 16-bit P holds too narrow a range for the speculative reference).
+  constexpr int kPasses = kBf16 ? 2 : 1;
+  // End of the speculative pass, for every warp that takes part (the whole warp calls it): true when the
+  // exact pass follows.
+  auto rerun_pass = [&]() {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->pass_sync);
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->pass_sync, 0, abort_flag));
+    return ok && *reinterpret_cast<volatile int*>(&bars->rerun) != 0 && *abort_flag == 0;
+  };
   if (warp < 4) {
     regs_dec<kRegsLow>();
     if (warp == 0) {
@@ -302,30 +506,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(smem + L::OFF_TH + c * L::kChunkBytes, &tmT, &bars->q_full, c * 16, I0);             // Th[I0..]
           tma_load_2d(smem + L::OFF_TW + c * L::kChunkBytes, &tmT, &bars->q_full, c * 16, 2 * kSide - 1);  // Tw
         }
-        int issued_k = 0, issued_v = 0;
+      }
+      // K and V of every key tile, once per pass; jj counts tiles over both passes (ring stage and parity)
+      int issued_k = 0, issued_v = 0;
+      auto load_pass = [&](int pass) {
+        if (lane != 0) return;
         for (int j = 0; j < kNT; ++j) {
-          const int st = j % kStages;
-          const uint32_t prev = ((j / kStages) - 1) & 1;
-          if (j >= kStages && !mbar_wait(&bars->k_empty[st], prev, abort_flag)) break;
+          const int jj = pass * kNT + j, st = jj % kStages;
+          const uint32_t prev = ((jj / kStages) - 1) & 1;
+          if (jj >= kStages && !mbar_wait(&bars->k_empty[st], prev, abort_flag)) break;
           mbar_arrive_expect_tx(&bars->k_full[st], L::kKBytes);
           for (int a = 0; a < 2; ++a)
             tma_load_2d(smem + L::OFF_K + st * L::kKBytes + a * L::kKAtom, &tmK, &bars->k_full[st],
                         j * kBK + a * 64, (int)(bh * HD));
-          issued_k = j + 1;
-          if (j >= kStages && !mbar_wait(&bars->v_empty[st], prev, abort_flag)) break;
+          issued_k = jj + 1;
+          if (jj >= kStages && !mbar_wait(&bars->v_empty[st], prev, abort_flag)) break;
           mbar_arrive_expect_tx(&bars->v_full[st], L::kVBytes);
           for (int c = 0; c < L::HC; ++c)
             tma_load_2d(smem + L::OFF_V + st * L::kVStage + c * L::kChunkBytes, &tmV, &bars->v_full[st], c * 16,
                         (int)(bh * kN + j * kBK));
-          issued_v = j + 1;
+          issued_v = jj + 1;
         }
-        if (*abort_flag) {
-          // drain this CTA's own copies still in flight before the CTA can exit
-          for (int j = issued_k > kStages ? issued_k - kStages : 0; j < issued_k; ++j)
-            mbar_drain(&bars->k_full[j % kStages], (j / kStages) & 1);
-          for (int j = issued_v > kStages ? issued_v - kStages : 0; j < issued_v; ++j)
-            mbar_drain(&bars->v_full[j % kStages], (j / kStages) & 1);
-        }
+      };
+      load_pass(0);
+      if (kPasses > 1 && rerun_pass()) load_pass(1);
+      if (lane == 0 && *abort_flag) {
+        // drain this CTA's own copies still in flight before the CTA can exit
+        for (int jj = issued_k > kStages ? issued_k - kStages : 0; jj < issued_k; ++jj)
+          mbar_drain(&bars->k_full[jj % kStages], (jj / kStages) & 1);
+        for (int jj = issued_v > kStages ? issued_v - kStages : 0; jj < issued_v; ++jj)
+          mbar_drain(&bars->v_full[jj % kStages], (jj / kStages) & 1);
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------------- MMA issuer
@@ -370,46 +580,56 @@ __global__ void __launch_bounds__(kThreads, 1)
         // S_q overwrites RW_q and the rh park aliases the tables: both query tiles must be done with them
         okk = wait(&bars->bias_done[0], 0) && wait(&bars->bias_done[1], 0) && wait(&bars->k_full[0], 0);
       }
-      if (okk) {
-        tc_fence_after();
-        issue_s(0, 0);
-        mma_commit_w(&bars->s_full[0]);
-        issue_s(1, 0);
-        mma_commit_w(&bars->s_full[1]);
-        mma_commit_w(&bars->k_empty[0]);
-      }
-      for (int j = 0; j < kNT && okk; ++j) {
-        const int st = j % kStages, st1 = (j + 1) % kStages;
-        const uint64_t dVs = desc_add(dV, st * L::kVStage);
-        const uint32_t acc0 = j > 0 ? 1u : 0u;
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          // the operands of this tile and of the next S (loaded long before; checked while the softmax
-          // still runs), then the softmax's P: PV_q(j) and S_q(j+1) issue back to back
-          if (q == 0) okk = wait(&bars->v_full[st], (j / kStages) & 1);
-          if (okk && q == 0 && j + 1 < kNT) okk = wait(&bars->k_full[st1], ((j + 1) / kStages) & 1);
-          if (okk) okk = wait(&bars->p_full[q], j & 1);
-          if (!okk) break;
+      // A pass takes 2 kNT / kStages phases of every ring barrier and kNT of the S- and P-ready ones, all
+      // even counts: the stages and parities of tile j are the same in both passes.
+      static_assert(kNT % (2 * kStages) == 0, "per-pass barrier phases must be even");
+      // one pass over the key tiles
+      auto issue_pass = [&](int pass) {
+        if (okk && pass > 0) okk = wait(&bars->k_full[0], 0);
+        if (okk) {
           tc_fence_after();
-#pragma unroll
-          for (int s = 0; s < kBK / 16; ++s)
-            mma_ts_w(tmem + 256 + q * L::kOCols, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV,
-                     s > 0 ? 1u : acc0);
-          if (j + 1 < kNT) {
-            // issued after PV_q(j), which reads P_q(j) from the same columns: in-order execution
-            issue_s(q, st1);
-            mma_commit_w(&bars->s_full[q]);
-          } else {
-            mma_commit_w(&bars->o_done[q]);
-          }
+          issue_s(0, 0);
+          mma_commit_w(&bars->s_full[0]);
+          issue_s(1, 0);
+          mma_commit_w(&bars->s_full[1]);
+          mma_commit_w(&bars->k_empty[0]);
         }
-        if (!okk) break;
-        mma_commit_w(&bars->v_empty[st]);
-        if (j + 1 < kNT) mma_commit_w(&bars->k_empty[st1]);
-      }
-      // every MMA issued by this warp has completed before the CTA tears down TMEM
-      mma_commit_w(&bars->final_mma);
-      mbar_drain(&bars->final_mma, 0);
+        for (int j = 0; j < kNT && okk; ++j) {
+          const int st = j % kStages, st1 = (j + 1) % kStages;
+          const uint64_t dVs = desc_add(dV, st * L::kVStage);
+          const uint32_t acc0 = j > 0 ? 1u : 0u;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            // the operands of this tile and of the next S (loaded long before; checked while the softmax
+            // still runs), then the softmax's P: PV_q(j) and S_q(j+1) issue back to back
+            if (q == 0) okk = wait(&bars->v_full[st], (j / kStages) & 1);
+            if (okk && q == 0 && j + 1 < kNT) okk = wait(&bars->k_full[st1], ((j + 1) / kStages) & 1);
+            if (okk) okk = wait(&bars->p_full[q], j & 1);
+            if (!okk) break;
+            tc_fence_after();
+#pragma unroll
+            for (int s = 0; s < kBK / 16; ++s)
+              mma_ts_w(tmem + 256 + q * L::kOCols, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV,
+                       s > 0 ? 1u : acc0);
+            if (j + 1 < kNT) {
+              // issued after PV_q(j), which reads P_q(j) from the same columns: in-order execution
+              issue_s(q, st1);
+              mma_commit_w(&bars->s_full[q]);
+            } else {
+              mma_commit_w(&bars->o_done[q]);
+            }
+          }
+          if (!okk) break;
+          mma_commit_w(&bars->v_empty[st]);
+          if (j + 1 < kNT) mma_commit_w(&bars->k_empty[st1]);
+        }
+        // every MMA issued by this warp has completed (before the next pass, or before the CTA tears down
+        // TMEM)
+        mma_commit_w(&bars->final_mma);
+        mbar_drain(&bars->final_mma, pass & 1);
+      };
+      issue_pass(0);
+      if (kPasses > 1 && rerun_pass()) issue_pass(1);
     }
   } else {
     regs_inc<kRegsHigh>();
@@ -472,117 +692,93 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->bias_done[q]);
     }
-    float mrA = -INFINITY, mrB = -INFINITY;
-    for (int j = 0; j < kNT && okk; ++j) {
-      okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
-      if (!okk) break;
-      tc_fence_after();
-      const float rhA0 = rh_park[(2 * j) * 256 + prowA], rhA1 = rh_park[(2 * j + 1) * 256 + prowA];
-      const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
-      // pass 1: row maxima of S*c + rw + rh (rh per 64-key half), then across the row's four threads
-      float tA, tB;
-      {
-        uint32_t v0[8], v1[8];
-        float mA[2] = {-INFINITY, -INFINITY}, mB[2] = {-INFINITY, -INFINITY};
-        static_for<0, 4>([&](auto kk) {
-          constexpr int k = decltype(kk)::value;  // chunks 2k and 2k+1 = blocks 4k .. 4k+3
-          tmem_ld_16x256b_x2(tS + 32 * k, v0);
-          tmem_ld_16x256b_x2(tS + 32 * k + 16, v1);
-          tmem_wait_ld_regs(v0);
-          tmem_wait_ld_regs(v1);
-          chunk_max<4 * k>(v0, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
-          chunk_max<4 * k + 2>(v1, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
-        });
-        tA = fmaxf(mA[0] + rhA0, mA[1] + rhA1);
-        tB = fmaxf(mB[0] + rhB0, mB[1] + rhB1);
-        tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 1));
-        tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 1));
-        tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 2));
-        tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 2));
-      }
-      const bool needA = (j == 0) || (tA > mrA + kRescaleThreshold);
-      const bool needB = (j == 0) || (tB > mrB + kRescaleThreshold);
-      float alA = 1.f, alB = 1.f;
-      if (needA) {
-        const float mn = fmaxf(mrA, tA);
-        alA = ex2(mrA - mn);
-        mrA = mn;
-      }
-      if (needB) {
-        const float mn = fmaxf(mrB, tB);
-        alB = ex2(mrB - mn);
-        mrB = mn;
-      }
-      // pass 2: p = 2^(S*c + rw + rh - m); P of chunk k (16-bit pairs, columns 8k..8k+7) lands on scores of
-      // chunk k/2 <= k, already read. The load of chunk k+1 is in flight meanwhile.
-      {
-        const float2 bA0 = make_float2(rhA0 - mrA, rhA0 - mrA), bA1 = make_float2(rhA1 - mrA, rhA1 - mrA);
-        const float2 bB0 = make_float2(rhB0 - mrB, rhB0 - mrB), bB1 = make_float2(rhB1 - mrB, rhB1 - mrB);
-        uint32_t v0[8], v1[8], pw[4];
-        tmem_ld_16x256b_x2(tS + 0, v0);
-        tmem_wait_ld_regs(v0);
-        static_for<0, 8>([&](auto kk) {
-          constexpr int k = decltype(kk)::value;  // chunk k = blocks 2k, 2k+1
-          uint32_t(&cur)[8] = (k & 1) ? v1 : v0;
-          uint32_t(&nxt)[8] = (k & 1) ? v0 : v1;
-          if constexpr (k + 1 < 8) tmem_ld_16x256b_x2(tS + 16 * (k + 1), nxt);
-          if constexpr (k < 4)
-            chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA0, bB0, pw);
-          else
-            chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA1, bB1, pw);
-          tmem_st_16x128b_x2(tS + 8 * k, pw);
-          if constexpr (k + 1 < 8) tmem_wait_ld_regs(nxt);
-        });
-      }
-      // O and row-sum rescale: PV_q(j-1) has completed (it was issued before S_q(j), whose commit we waited
-      // on).
-      if (__any_sync(0xffffffffu, (needA || needB) && j > 0)) {
+    // pass 2 over the tile with reference maxima (mrA, mrB): p = 2^(S*c + rw + rh - m); P of chunk k (16-bit
+    // pairs, columns 8k..8k+7) lands on scores of chunk k/2 <= k, already read. The load of chunk k+1 is in
+    // flight meanwhile. TRACK: the largest exponent per (row, 64-key half) into xm (A0, A1, B0, B1).
+    SoftmaxRows<T, HD> sm;
+    sm.tS = tS;
+    sm.tO = tO;
+    sm.c2 = c2;
 #pragma unroll
-        for (int c0 = 0; c0 < L::kOCols; c0 += 16) {
-          uint32_t ov[8];
-          tmem_ld_16x256b_x2(tO + c0, ov);
-          tmem_wait_ld_regs(ov);
-          ov[0] = __float_as_uint(__uint_as_float(ov[0]) * alA);
-          ov[1] = __float_as_uint(__uint_as_float(ov[1]) * alA);
-          ov[4] = __float_as_uint(__uint_as_float(ov[4]) * alA);
-          ov[5] = __float_as_uint(__uint_as_float(ov[5]) * alA);
-          ov[2] = __float_as_uint(__uint_as_float(ov[2]) * alB);
-          ov[3] = __float_as_uint(__uint_as_float(ov[3]) * alB);
-          ov[6] = __float_as_uint(__uint_as_float(ov[6]) * alB);
-          ov[7] = __float_as_uint(__uint_as_float(ov[7]) * alB);
-          tmem_st_16x256b_x2(tO + c0, ov);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();  // every lane's P and O stores are complete: one arrival per warp
-      if (lane == 0) mbar_arrive(&bars->p_full[q]);
+    for (int m = 0; m < 8; ++m) {
+      sm.rwA[m] = rwA[m];
+      sm.rwB[m] = rwB[m];
     }
-    // epilogue: O / l -> out, once PV_q of the last tile has completed
-    if (okk) okk = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[q], 0, abort_flag));
-    if (okk) {
-      tc_fence_after();
-      // every column of the ones block holds the row sum
-      uint32_t lv[8];
-      tmem_ld_16x256b_x2(tO + HD, lv);
-      tmem_wait_ld_regs(lv);
-      const float invA = 1.f / __uint_as_float(lv[0]), invB = 1.f / __uint_as_float(lv[2]);
-      T* oA = out + (bh * kN + row0 + prowA) * HD + 2 * c;
-      T* oB = oA + 8 * HD;
-#pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 16) {
-        uint32_t ov[8];
-        tmem_ld_16x256b_x2(tO + c0, ov);
-        tmem_wait_ld_regs(ov);
-        *reinterpret_cast<uint32_t*>(oA + c0) =
-            pack2(__uint_as_float(ov[0]) * invA, __uint_as_float(ov[1]) * invA, kBf16);
-        *reinterpret_cast<uint32_t*>(oA + c0 + 8) =
-            pack2(__uint_as_float(ov[4]) * invA, __uint_as_float(ov[5]) * invA, kBf16);
-        *reinterpret_cast<uint32_t*>(oB + c0) =
-            pack2(__uint_as_float(ov[2]) * invB, __uint_as_float(ov[3]) * invB, kBf16);
-        *reinterpret_cast<uint32_t*>(oB + c0 + 8) =
-            pack2(__uint_as_float(ov[6]) * invB, __uint_as_float(ov[7]) * invB, kBf16);
+    sm.rh_park = rh_park;
+    sm.prowA = prowA;
+    sm.prowB = prowB;
+    sm.bars = bars;
+    sm.q = q;
+    sm.lane = lane;
+    sm.oA = out + (bh * kN + row0 + prowA) * HD + 2 * c;
+    sm.abort_flag = abort_flag;
+    if constexpr (!kBf16) {
+      if (okk) sm.exact_pass(0);
+    } else {
+      // Speculative pass (bf16): the first tile exact, the others in a single pass. Per row: run = the
+      // running max of the full score, base = that of S*c + rw (without the per-key-row rh term), rhmax =
+      // the largest rh over all key rows. base + rhmax bounds a tile's max unless the base grows within it;
+      // the prediction is that bound capped kSpecCap above run, and the reference is raised to it once it
+      // passes the reference by kSpecRaise. Any reference gives the same softmax (O and its row sums scale
+      // together), and bf16 P and the f32 sums hold 2^-126 .. 2^127: the exponents are tracked, and if one
+      // exceeds kSpecLimit or an output is not finite, the CTA runs the exact pass.
+      float runA, runB, baseA, baseB, rhmaxA = -INFINITY, rhmaxB = -INFINITY;
+      bool unsafe = false;
+      sm.mrA = -INFINITY;
+      sm.mrB = -INFINITY;
+      for (int j = 0; j < kNT && okk; ++j) {
+        okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
+        if (!okk) break;
+        tc_fence_after();
+        const float rhA0 = sm.rh(2 * j, prowA), rhA1 = sm.rh(2 * j + 1, prowA);
+        const float rhB0 = sm.rh(2 * j, prowB), rhB1 = sm.rh(2 * j + 1, prowB);
+        bool needA, needB;
+        float alA = 1.f, alB = 1.f;
+        if (j == 0) {
+#pragma unroll 8
+          for (int kh = 0; kh < 64; ++kh) {
+            rhmaxA = fmaxf(rhmaxA, sm.rh(kh, prowA));
+            rhmaxB = fmaxf(rhmaxB, sm.rh(kh, prowB));
+          }
+          sm.template exact_tile<true>(j, rhA0, rhA1, rhB0, rhB1, alA, alB, needA, needB, runA, runB, baseA,
+                                       baseB);
+        } else {
+          const float pA = fminf(baseA + rhmaxA, runA + kSpecCap), pB = fminf(baseB + rhmaxB, runB + kSpecCap);
+          needA = pA > sm.mrA + kSpecRaise;
+          needB = pB > sm.mrB + kSpecRaise;
+          if (needA) {
+            alA = ex2(sm.mrA - pA);
+            sm.mrA = pA;
+          }
+          if (needB) {
+            alB = ex2(sm.mrB - pB);
+            sm.mrB = pB;
+          }
+          float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+          sm.template pass2<true>(rhA0, rhA1, rhB0, rhB1, xm);
+          unsafe |= fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])) > kSpecLimit;
+          // the tile's base and max: the exponent maxima + m (- rh), across the row's four threads
+          float bA = fmaxf(xm[0] - rhA0, xm[1] - rhA1) + sm.mrA, bB = fmaxf(xm[2] - rhB0, xm[3] - rhB1) + sm.mrB;
+          float uA = fmaxf(xm[0], xm[1]) + sm.mrA, uB = fmaxf(xm[2], xm[3]) + sm.mrB;
+          bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 1));
+          bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 1));
+          uA = fmaxf(uA, __shfl_xor_sync(0xffffffffu, uA, 1));
+          uB = fmaxf(uB, __shfl_xor_sync(0xffffffffu, uB, 1));
+          bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 2));
+          bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 2));
+          uA = fmaxf(uA, __shfl_xor_sync(0xffffffffu, uA, 2));
+          uB = fmaxf(uB, __shfl_xor_sync(0xffffffffu, uB, 2));
+          baseA = fmaxf(baseA, bA);
+          baseB = fmaxf(baseB, bB);
+          runA = fmaxf(runA, uA);
+          runB = fmaxf(runB, uB);
+        }
+        sm.finish_tile(j, needA, needB, alA, alB);
       }
+      bool finite = true;
+      if (okk) okk = sm.epilogue(0, finite);
+      if (__any_sync(0xffffffffu, unsafe || !finite) && lane == 0) bars->rerun = 1;
+      if (rerun_pass()) softmax_rerun<T, HD>(sm);
     }
   }
   tc_fence_before();

@@ -128,13 +128,14 @@ def test_global_late_max_jumps(samrs, cuda, hd, dt):
     Every query has a large first coordinate and a few keys have a large first coordinate, so that a
     query's max logit jumps by 25 to 30 log2 units at a later 128-key tile (far beyond the largest P a
     16-bit type holds against the earlier reference): in the first tiles, in the middle, and in the last
-    tile only, per head. Most rows end up dominated by one key, whose 16-bit P rounding must cancel
-    between the numerator and the row sum."""
+    tile only, per head; head 1 jumps by ~130 in the last tile (beyond an f32 P against the earlier
+    reference: the bf16 single-pass CTA must be recomputed). Most rows end up dominated by one key, whose
+    16-bit P rounding must cancel between the numerator and the row sum."""
     h = w = 64
     q, kt, v, t = make_inputs(h, w, 3, hd, seed=hd + 5, table_std=0.5)
     q[:, :, 0] = 4.0
     jumps = {0: {128 * 1 + 3: 40.0, 128 * 9 + 77: 80.0, 128 * 31 + 127: 120.0},
-             1: {128 * 31 + 5: 80.0},
+             1: {128 * 31 + 5: 200.0},
              2: {128 * 2 + 64: 40.0, 128 * 3 + 1: 80.0, 128 * 4 + 2: 120.0, 128 * 20 + 90: 160.0}}
     for b, keys in jumps.items():
         for key, big in keys.items():
@@ -145,6 +146,30 @@ def test_global_late_max_jumps(samrs, cuda, hd, dt):
     assert samrs.device_status() == 0
     ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, w, scale)
     err = parity_err(out.float().cpu().numpy(), ref, dt)
+    assert err < HALF_TOL, err
+
+
+@pytest.mark.parametrize("hd", [64, 80])
+def test_global_bf16_overflow_recompute(samrs, cuda, hd):
+    """bf16 global layers: a CTA whose single-pass tiles would overflow is recomputed exactly.
+
+    v ~ 1e35 and, per head, one key in a later tile whose logit jumps ~25-29 log2 units above the running
+    max: the single-pass tile's P of that key reaches ~2^25, P.V overflows f32, and the CTA must take the
+    exact pass (P <= 2^8 there, so O stays finite)."""
+    h = w = 64
+    q, kt, v, t = make_inputs(h, w, 2, hd, seed=hd + 11, table_std=0.5)
+    q[:, :, 0] = 4.0
+    v *= 1e35
+    kt[0, 0, 128 * 5 + 17] = 40.0
+    kt[1, 0, 128 * 30 + 101] = 40.0
+    scale = hd ** -0.5
+    qd, ktd, vd, td = (to_dev(x, "bf16", cuda) for x in (q, kt, v, t))
+    out = samrs.attention_relpos(qd, ktd, vd, td, h, w, scale)
+    assert samrs.device_status() == 0
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, w, scale)
+    err = parity_err(got, ref, "bf16")
     assert err < HALF_TOL, err
 
 
