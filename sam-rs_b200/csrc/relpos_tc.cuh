@@ -96,12 +96,20 @@ int tc_launch_global(const void* q, const void* kt, const void* v, const void* t
   if (!rc) rc = make_map(&mv, bf16, v, HD, (uint64_t)bh * kN, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B);
   if (!rc) rc = make_map(&mt, bf16, table, HD, 4 * kSide - 2, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
-  auto kern = relpos_attn_global<T, HD>;
-  static const bool regs_ok = regs_cover_split(kern, kThreads, 128 * kRegsLow + 512 * kRegsHigh);
+  // f16: the exact kernel. bf16: the speculative kernel, then the fixup launch, which recomputes exactly
+  // the CTAs the first one marked (the others return at once).
+  auto first = relpos_attn_global<T, HD, bf16 ? kModeSpec : kModeExact>;
+  auto fixup = relpos_attn_global<T, HD, bf16 ? kModeFixup : kModeExact>;
+  const int split = 128 * kRegsLow + 512 * kRegsHigh;
+  static const bool regs_ok = regs_cover_split(first, kThreads, split) && regs_cover_split(fixup, kThreads, split);
   if (!regs_ok) return 6;
   const int smem = Layout<HD>::kSmemBytes;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return 5;
-  kern<<<(unsigned)(bh * (kN / 256)), kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale);
+  if (cudaFuncSetAttribute(first, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaFuncSetAttribute(fixup, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return 5;
+  const unsigned grid = (unsigned)(bh * (kN / 256));
+  first<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale);
+  if (bf16) fixup<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale);
   return 0;
 }
 

@@ -8,29 +8,34 @@
 // One CTA = one head (bh) x 256 query rows (two 128-row tiles Q0, Q1 = grid rows I0..I0+3), looping
 // over 32 key tiles of 128 keys (grid rows kh = 2t, 2t+1); both query tiles share every K/V tile.
 // 20 warps:
-//   warp 0       TMA producer: Q0, Q1 and the two table slices once, then K and V tiles (3-stage rings)
-//   warp 1       MMA issuer (one thread): prologue bias MMAs, then per tile and query tile, in order,
-//                O_q += P_q(t) V(t) and S_q(t+1) = Q_q K(t+1)^T. In-order issue lets S_q(t+1) overwrite
-//                P_q(t) (both live in the S_q columns) without a round trip through a barrier.
+//   warp 0       TMA producer: Q0, Q1 and the two table slices once, then K and V tiles (2-stage rings)
+//   warp 1       MMA issuer (the warp runs the loop, lane 0 issues): prologue bias MMAs, then per tile and
+//                query tile, in order, O_q += P_q(t) [V(t) | 1] and S_q(t+1) = Q_q K(t+1)^T. In-order issue
+//                lets S_q(t+1) overwrite P_q(t) (both live in the S_q columns) without a round trip through
+//                a barrier.
 //   warp 2       TMEM allocator (512 columns)
 //   warps 4-11   softmax of Q0, warps 12-19 softmax of Q1: two warps per TMEM lane quarter, one per
 //                16-lane half. With the 16x256b access shape four threads share a row pair (rows r and
 //                r+8 of the half), each holding key pairs 8m + 2(t%4), +1: 64 scores per thread and
-//                tile, row maxima and sums combined with two shuffles. Four softmax warps per SM
-//                sub-partition keep the exp unit busy while the other query tile waits on its MMAs.
+//                tile, row maxima combined with two shuffles. Four softmax warps per SM sub-partition keep
+//                the exp unit busy while the other query tile waits on its MMAs.
 //
 // Rel-pos bias, computed in-tile: the prologue MMAs give RW = Q Tw^T (128 cols) and RH = Q Th[I0..I0+79]^T
 // (80 cols) in TMEM. rw: each warp reads RW for its lane quarter, a lane-dependent barrel shift selects
 // row r's window j..j+63 (reversed, = rw[kw]) and shuffles hand each thread the 16 values of its key
 // pairs for its two rows (log2 units, in registers). rh: parked in shared memory as [kh][row]; a key tile
 // needs two rh values per row (one per 64-key half).
-// The softmax is online in the log2 domain with conditional rescaling (O is rescaled only when the row
-// max grows by more than 8); P is written back as 16-bit pairs into the S columns of TMEM and fed to the
-// PV MMA as the A operand straight from TMEM. No score ever reaches HBM.
+// The softmax is online in the log2 domain; P is written back as 16-bit pairs into the S columns of TMEM
+// and fed to the P.V MMA as the A operand straight from TMEM. The V stages carry a block of ones, so the
+// MMA also accumulates the row sums of P as rounded. Exact mode (f16): two passes per tile, O rescaled only
+// when the row max grows by more than 8. Speculative mode (bf16): one pass per tile after the first,
+// against a predicted max; a CTA that overflows leaves a NaN marker and is recomputed by the fixup mode
+// (exact, marked CTAs only) launched right after. No score ever reaches HBM.
 //
-// TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O0 [256,256+HD), O1 [256+HD, 256+2HD); prologue:
-// RW_q in S_q, RH_q at [256+80q, 256+80q+80).
-// Shared memory (1 KB aligned): Q0 | Q1 | K ring | V ring | RH park (tables alias it in the prologue) | barriers.
+// TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O0 and its row sums [256, 256+HD+16), O1 after it;
+// prologue: RW_q in S_q, RH_q at [256+80q, 256+80q+80).
+// Shared memory (1 KB aligned): Q0 | Q1 | K ring | V ring (each stage: v, then ones) | RH park (tables
+// alias it in the prologue) | barriers.
 #pragma once
 #include <cuda.h>
 
@@ -53,8 +58,13 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 // bf16: speculative single-pass tiles (see the softmax). The predicted max is capped kSpecCap above the
 // row's running max, the reference is raised once the prediction passes it by kSpecRaise, and a CTA whose
-// tiles saw an exponent above kSpecLimit (P > 2^64) or a non-finite output is recomputed exactly.
+// tiles saw an exponent above kSpecLimit (P > 2^64) or a non-finite output is recomputed exactly by a
+// second launch.
 constexpr float kSpecCap = 64.f, kSpecRaise = 4.f, kSpecLimit = 64.f;
+// Kernel modes: the exact two-pass softmax (f16); the speculative pass (bf16), which marks a CTA that needs
+// the exact pass by a NaN in the first element of its output block; the exact pass of the marked CTAs
+// only (bf16, launched right after the speculative one; the others return at once).
+constexpr int kModeExact = 0, kModeSpec = 1, kModeFixup = 2;
 
 template <int HD>
 struct Layout {
@@ -87,10 +97,10 @@ struct Bars {
   uint64_t q_full, pro_done, final_mma;
   uint64_t k_full[kStages], v_full[kStages], k_empty[kStages], v_empty[kStages];
   uint64_t bias_done[2], s_full[2], p_full[2], o_done[2];
-  uint64_t pass_sync;  // bf16: end of the speculative pass (producer, issuer and the 16 softmax warps)
+  uint64_t epi_done;  // speculative pass: every softmax warp has written its outputs and flag
   uint32_t tmem_base;
   int abort_flag;
-  int rerun;  // bf16: a softmax thread asks for the exact pass
+  int rerun;  // speculative pass: a softmax thread asks for the exact pass
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
 
@@ -238,186 +248,7 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, con
   }
 }
 
-// State of one softmax thread: its two rows (A, B) of query tile q, their rw registers and the running
-// reference maxima. The tile steps are inline; the exact pass of a rerun is a separate function that gets
-// the state by value, so that the speculative loop keeps its registers.
-template <typename T, int HD>
-struct SoftmaxRows {
-  static constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  using L = Layout<HD>;
-  uint32_t tS, tO;         // this warp's S/P and O columns (lane base included)
-  float2 c2;               // scale * log2(e), twice
-  float2 rwA[8], rwB[8];   // rw of rows A and B for this thread's key pairs (log2 units)
-  const float* rh_park;    // rh per (key row, tile row)
-  int prowA, prowB;        // the rows within the CTA's 256
-  Bars* bars;
-  int q, lane;
-  T* oA;                   // output row A at this thread's column pair; row B is 8 rows further
-  volatile int* abort_flag;
-  float mrA, mrB;          // reference maxima
-
-  __device__ __forceinline__ float rh(int kh, int prow) const { return rh_park[kh * 256 + prow]; }
-
-  // Pass 2 over the tile with reference maxima (mrA, mrB): p = 2^(S*c + rw + rh - m); P of chunk k (16-bit
-  // pairs, columns 8k..8k+7) lands on scores of chunk k/2 <= k, already read. The load of chunk k+1 is in
-  // flight meanwhile. TRACK: the largest exponent per (row, 64-key half) into xm (A0, A1, B0, B1).
-  template <bool TRACK>
-  __device__ __forceinline__ void pass2(float rhA0, float rhA1, float rhB0, float rhB1, float (&xm)[4]) {
-    using namespace sm100;
-    const float2 bA0 = make_float2(rhA0 - mrA, rhA0 - mrA), bA1 = make_float2(rhA1 - mrA, rhA1 - mrA);
-    const float2 bB0 = make_float2(rhB0 - mrB, rhB0 - mrB), bB1 = make_float2(rhB1 - mrB, rhB1 - mrB);
-    uint32_t v0[8], v1[8], pw[4];
-    tmem_ld_16x256b_x2(tS + 0, v0);
-    tmem_wait_ld_regs(v0);
-    static_for<0, 8>([&](auto kk) {
-      constexpr int k = decltype(kk)::value;  // chunk k = blocks 2k, 2k+1
-      uint32_t(&cur)[8] = (k & 1) ? v1 : v0;
-      uint32_t(&nxt)[8] = (k & 1) ? v0 : v1;
-      if constexpr (k + 1 < 8) tmem_ld_16x256b_x2(tS + 16 * (k + 1), nxt);
-      if constexpr (k < 4)
-        chunk_exp<2 * k, kBf16, TRACK>(cur, c2, rwA, rwB, bA0, bB0, pw, xm[0], xm[2]);
-      else
-        chunk_exp<2 * k, kBf16, TRACK>(cur, c2, rwA, rwB, bA1, bB1, pw, xm[1], xm[3]);
-      tmem_st_16x128b_x2(tS + 8 * k, pw);
-      if constexpr (k + 1 < 8) tmem_wait_ld_regs(nxt);
-    });
-  }
-
-  // Exact tile: pass 1 gives the row maxima t of S*c + rw + rh (rh per 64-key half) across the row's four
-  // threads (BASE: also those of S*c + rw), the reference is raised if needed, then pass 2.
-  template <bool BASE>
-  __device__ __forceinline__ void exact_tile(int j, float rhA0, float rhA1, float rhB0, float rhB1, float& alA,
-                                             float& alB, bool& needA, bool& needB, float& tA, float& tB,
-                                             float& bA, float& bB) {
-    using namespace sm100;
-    {
-      uint32_t v0[8], v1[8];
-      float mA[2] = {-INFINITY, -INFINITY}, mB[2] = {-INFINITY, -INFINITY};
-      static_for<0, 4>([&](auto kk) {
-        constexpr int k = decltype(kk)::value;  // chunks 2k and 2k+1 = blocks 4k .. 4k+3
-        tmem_ld_16x256b_x2(tS + 32 * k, v0);
-        tmem_ld_16x256b_x2(tS + 32 * k + 16, v1);
-        tmem_wait_ld_regs(v0);
-        tmem_wait_ld_regs(v1);
-        chunk_max<4 * k>(v0, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
-        chunk_max<4 * k + 2>(v1, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
-      });
-      tA = fmaxf(mA[0] + rhA0, mA[1] + rhA1);
-      tB = fmaxf(mB[0] + rhB0, mB[1] + rhB1);
-      tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 1));
-      tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 1));
-      tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 2));
-      tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 2));
-      if constexpr (BASE) {
-        bA = fmaxf(mA[0], mA[1]);
-        bB = fmaxf(mB[0], mB[1]);
-        bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 1));
-        bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 1));
-        bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 2));
-        bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 2));
-      }
-    }
-    needA = (j == 0) || (tA > mrA + kRescaleThreshold);
-    needB = (j == 0) || (tB > mrB + kRescaleThreshold);
-    if (needA) {
-      const float mn = fmaxf(mrA, tA);
-      alA = ex2(mrA - mn);
-      mrA = mn;
-    }
-    if (needB) {
-      const float mn = fmaxf(mrB, tB);
-      alB = ex2(mrB - mn);
-      mrB = mn;
-    }
-    float xm[4];
-    pass2<false>(rhA0, rhA1, rhB0, rhB1, xm);
-  }
-
-  // End of a tile: O and row-sum rescale (PV_q(j-1) has completed: it was issued before S_q(j), whose
-  // commit was waited on), then one P-ready arrival per warp once every lane's P and O stores are done.
-  __device__ __forceinline__ void finish_tile(int j, bool needA, bool needB, float alA, float alB) {
-    using namespace sm100;
-    if (__any_sync(0xffffffffu, (needA || needB) && j > 0)) {
-#pragma unroll
-      for (int c0 = 0; c0 < L::kOCols; c0 += 16) {
-        uint32_t ov[8];
-        tmem_ld_16x256b_x2(tO + c0, ov);
-        tmem_wait_ld_regs(ov);
-        ov[0] = __float_as_uint(__uint_as_float(ov[0]) * alA);
-        ov[1] = __float_as_uint(__uint_as_float(ov[1]) * alA);
-        ov[4] = __float_as_uint(__uint_as_float(ov[4]) * alA);
-        ov[5] = __float_as_uint(__uint_as_float(ov[5]) * alA);
-        ov[2] = __float_as_uint(__uint_as_float(ov[2]) * alB);
-        ov[3] = __float_as_uint(__uint_as_float(ov[3]) * alB);
-        ov[6] = __float_as_uint(__uint_as_float(ov[6]) * alB);
-        ov[7] = __float_as_uint(__uint_as_float(ov[7]) * alB);
-        tmem_st_16x256b_x2(tO + c0, ov);
-      }
-    }
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&bars->p_full[q]);
-  }
-
-  // Epilogue of a pass: O / l -> out once PV_q of the last tile has completed (l = any column of the ones
-  // block). Returns false if the pass was aborted; `finite` is cleared if an output is inf or NaN.
-  __device__ __forceinline__ bool epilogue(int pass, bool& finite) {
-    using namespace sm100;
-    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[q], pass & 1, abort_flag))) return false;
-    tc_fence_after();
-    uint32_t lv[8];
-    tmem_ld_16x256b_x2(tO + HD, lv);
-    tmem_wait_ld_regs(lv);
-    const float invA = 1.f / __uint_as_float(lv[0]), invB = 1.f / __uint_as_float(lv[2]);
-    T* oB = oA + 8 * HD;
-#pragma unroll
-    for (int c0 = 0; c0 < HD; c0 += 16) {
-      uint32_t ov[8];
-      tmem_ld_16x256b_x2(tO + c0, ov);
-      tmem_wait_ld_regs(ov);
-      float y[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        y[e] = __uint_as_float(ov[e]) * ((e & 2) ? invB : invA);
-        finite &= fabsf(y[e]) < INFINITY;  // false for inf and NaN
-      }
-      *reinterpret_cast<uint32_t*>(oA + c0) = pack2(y[0], y[1], kBf16);
-      *reinterpret_cast<uint32_t*>(oA + c0 + 8) = pack2(y[4], y[5], kBf16);
-      *reinterpret_cast<uint32_t*>(oB + c0) = pack2(y[2], y[3], kBf16);
-      *reinterpret_cast<uint32_t*>(oB + c0 + 8) = pack2(y[6], y[7], kBf16);
-    }
-    return true;
-  }
-
-  // The exact pass over all key tiles, then the epilogue. kNT is even, so the S-ready and P-ready parities
-  // of tile j are the same in both passes. Returns false if it was aborted.
-  __device__ __forceinline__ bool exact_pass(int pass) {
-    using namespace sm100;
-    mrA = -INFINITY;
-    mrB = -INFINITY;
-    for (int j = 0; j < kNT; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag))) return false;
-      tc_fence_after();
-      bool needA, needB;
-      float alA = 1.f, alB = 1.f, tA, tB, bA, bB;
-      exact_tile<false>(j, rh(2 * j, prowA), rh(2 * j + 1, prowA), rh(2 * j, prowB), rh(2 * j + 1, prowB), alA,
-                        alB, needA, needB, tA, tB, bA, bB);
-      finish_tile(j, needA, needB, alA, alB);
-    }
-    bool finite = true;
-    return epilogue(pass, finite);
-  }
-};
-
-// The exact pass of a bf16 CTA whose speculative pass asked for it (rare): out of line, on a copy of the
-// state.
-template <typename T, int HD>
-__device__ __noinline__ bool softmax_rerun(SoftmaxRows<T, HD> rows) {
-  return rows.exact_pass(1);
-}
-
-template <typename T, int HD>
+template <typename T, int HD, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     relpos_attn_global(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmT,
@@ -425,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = Layout<HD>;
   using namespace sm100;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  static_assert(MODE == kModeExact || kBf16, "the speculative pass and its fixup are bf16 only");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + L::OFF_BAR);
@@ -437,6 +269,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ct = blockIdx.x % (kN / 256);
   const int row0 = ct * 256;  // first query row of the CTA
   const int I0 = ct * 4;      // its first grid row
+  T* const marker = out + (bh * kN + row0) * HD;  // first element of the CTA's output block
+  if constexpr (MODE == kModeFixup) {
+    // only CTAs whose speculative pass left the NaN marker (the same value for every thread)
+    const float m = to_f(*reinterpret_cast<volatile T*>(marker));
+    if (!(m != m)) return;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -454,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->p_full[q], 8);
       mbar_init(&bars->o_done[q], 1);
     }
-    mbar_init(&bars->pass_sync, 18);
+    mbar_init(&bars->epi_done, 16);  // one arrival per softmax warp
     bars->abort_flag = 0;
     bars->rerun = 0;
     fence_mbar_init();
@@ -477,17 +315,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  // bf16 runs the speculative pass first and, for a CTA that asks for it, the exact pass; f16 runs the
-  // exact pass only (its 16-bit P holds too narrow a range for the speculative reference).
-  constexpr int kPasses = kBf16 ? 2 : 1;
-  // End of the speculative pass, for every warp that takes part (the whole warp calls it): true when the
-  // exact pass follows.
-  auto rerun_pass = [&]() {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&bars->pass_sync);
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->pass_sync, 0, abort_flag));
-    return ok && *reinterpret_cast<volatile int*>(&bars->rerun) != 0 && *abort_flag == 0;
-  };
   if (warp < 4) {
     regs_dec<kRegsLow>();
     if (warp == 0) {
@@ -507,12 +334,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(smem + L::OFF_TW + c * L::kChunkBytes, &tmT, &bars->q_full, c * 16, 2 * kSide - 1);  // Tw
         }
       }
-      // K and V of every key tile, once per pass; jj counts tiles over both passes (ring stage and parity)
+      // K and V of every key tile
       int issued_k = 0, issued_v = 0;
-      auto load_pass = [&](int pass) {
-        if (lane != 0) return;
+      if (lane == 0) {
         for (int j = 0; j < kNT; ++j) {
-          const int jj = pass * kNT + j, st = jj % kStages;
+          const int jj = j, st = jj % kStages;
           const uint32_t prev = ((jj / kStages) - 1) & 1;
           if (jj >= kStages && !mbar_wait(&bars->k_empty[st], prev, abort_flag)) break;
           mbar_arrive_expect_tx(&bars->k_full[st], L::kKBytes);
@@ -527,9 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         (int)(bh * kN + j * kBK));
           issued_v = jj + 1;
         }
-      };
-      load_pass(0);
-      if (kPasses > 1 && rerun_pass()) load_pass(1);
+      }
       if (lane == 0 && *abort_flag) {
         // drain this CTA's own copies still in flight before the CTA can exit
         for (int jj = issued_k > kStages ? issued_k - kStages : 0; jj < issued_k; ++jj)
@@ -580,12 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // S_q overwrites RW_q and the rh park aliases the tables: both query tiles must be done with them
         okk = wait(&bars->bias_done[0], 0) && wait(&bars->bias_done[1], 0) && wait(&bars->k_full[0], 0);
       }
-      // A pass takes 2 kNT / kStages phases of every ring barrier and kNT of the S- and P-ready ones, all
-      // even counts: the stages and parities of tile j are the same in both passes.
-      static_assert(kNT % (2 * kStages) == 0, "per-pass barrier phases must be even");
-      // one pass over the key tiles
-      auto issue_pass = [&](int pass) {
-        if (okk && pass > 0) okk = wait(&bars->k_full[0], 0);
+      {
         if (okk) {
           tc_fence_after();
           issue_s(0, 0);
@@ -623,13 +442,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit_w(&bars->v_empty[st]);
           if (j + 1 < kNT) mma_commit_w(&bars->k_empty[st1]);
         }
-        // every MMA issued by this warp has completed (before the next pass, or before the CTA tears down
-        // TMEM)
+        // every MMA issued by this warp has completed before the CTA tears down TMEM
         mma_commit_w(&bars->final_mma);
-        mbar_drain(&bars->final_mma, pass & 1);
-      };
-      issue_pass(0);
-      if (kPasses > 1 && rerun_pass()) issue_pass(1);
+        mbar_drain(&bars->final_mma, 0);
+      }
     }
   } else {
     regs_inc<kRegsHigh>();
@@ -695,71 +511,194 @@ __global__ void __launch_bounds__(kThreads, 1)
     // pass 2 over the tile with reference maxima (mrA, mrB): p = 2^(S*c + rw + rh - m); P of chunk k (16-bit
     // pairs, columns 8k..8k+7) lands on scores of chunk k/2 <= k, already read. The load of chunk k+1 is in
     // flight meanwhile. TRACK: the largest exponent per (row, 64-key half) into xm (A0, A1, B0, B1).
-    SoftmaxRows<T, HD> sm;
-    sm.tS = tS;
-    sm.tO = tO;
-    sm.c2 = c2;
+    float mrA = -INFINITY, mrB = -INFINITY;
+    auto pass2 = [&](auto track, float rhA0, float rhA1, float rhB0, float rhB1, float (&xm)[4]) {
+      constexpr bool kTrack = decltype(track)::value;
+      const float2 bA0 = make_float2(rhA0 - mrA, rhA0 - mrA), bA1 = make_float2(rhA1 - mrA, rhA1 - mrA);
+      const float2 bB0 = make_float2(rhB0 - mrB, rhB0 - mrB), bB1 = make_float2(rhB1 - mrB, rhB1 - mrB);
+      uint32_t v0[8], v1[8], pw[4];
+      tmem_ld_16x256b_x2(tS + 0, v0);
+      tmem_wait_ld_regs(v0);
+      static_for<0, 8>([&](auto kk) {
+        constexpr int k = decltype(kk)::value;  // chunk k = blocks 2k, 2k+1
+        uint32_t(&cur)[8] = (k & 1) ? v1 : v0;
+        uint32_t(&nxt)[8] = (k & 1) ? v0 : v1;
+        if constexpr (k + 1 < 8) tmem_ld_16x256b_x2(tS + 16 * (k + 1), nxt);
+        if constexpr (k < 4)
+          chunk_exp<2 * k, kBf16, kTrack>(cur, c2, rwA, rwB, bA0, bB0, pw, xm[0], xm[2]);
+        else
+          chunk_exp<2 * k, kBf16, kTrack>(cur, c2, rwA, rwB, bA1, bB1, pw, xm[1], xm[3]);
+        tmem_st_16x128b_x2(tS + 8 * k, pw);
+        if constexpr (k + 1 < 8) tmem_wait_ld_regs(nxt);
+      });
+    };
+    // Exact tile: pass 1 gives the row maxima t of S*c + rw + rh (rh per 64-key half) across the row's four
+    // threads (and, if base is given, the maxima of S*c + rw), then pass 2 against the raised reference.
+    auto exact_tile = [&](int j, float rhA0, float rhA1, float rhB0, float rhB1, float& alA, float& alB,
+                          bool& needA, bool& needB, float& tA, float& tB, float* bA_out, float* bB_out) {
+      {
+        uint32_t v0[8], v1[8];
+        float mA[2] = {-INFINITY, -INFINITY}, mB[2] = {-INFINITY, -INFINITY};
+        static_for<0, 4>([&](auto kk) {
+          constexpr int k = decltype(kk)::value;  // chunks 2k and 2k+1 = blocks 4k .. 4k+3
+          tmem_ld_16x256b_x2(tS + 32 * k, v0);
+          tmem_ld_16x256b_x2(tS + 32 * k + 16, v1);
+          tmem_wait_ld_regs(v0);
+          tmem_wait_ld_regs(v1);
+          chunk_max<4 * k>(v0, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
+          chunk_max<4 * k + 2>(v1, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
+        });
+        tA = fmaxf(mA[0] + rhA0, mA[1] + rhA1);
+        tB = fmaxf(mB[0] + rhB0, mB[1] + rhB1);
+        tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 1));
+        tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 1));
+        tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 2));
+        tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 2));
+        if (bA_out) {
+          float bA = fmaxf(mA[0], mA[1]), bB = fmaxf(mB[0], mB[1]);
+          bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 1));
+          bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 1));
+          bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 2));
+          bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 2));
+          *bA_out = bA;
+          *bB_out = bB;
+        }
+      }
+      needA = (j == 0) || (tA > mrA + kRescaleThreshold);
+      needB = (j == 0) || (tB > mrB + kRescaleThreshold);
+      if (needA) {
+        const float mn = fmaxf(mrA, tA);
+        alA = ex2(mrA - mn);
+        mrA = mn;
+      }
+      if (needB) {
+        const float mn = fmaxf(mrB, tB);
+        alB = ex2(mrB - mn);
+        mrB = mn;
+      }
+      float xm[4];
+      pass2(std::integral_constant<bool, false>{}, rhA0, rhA1, rhB0, rhB1, xm);
+    };
+    // End of a tile: O and row-sum rescale (PV_q(j-1) has completed: it was issued before S_q(j), whose
+    // commit we waited on), then one P-ready arrival per warp once every lane's P and O stores are done.
+    auto finish_tile = [&](int j, bool needA, bool needB, float alA, float alB) {
+      if (__any_sync(0xffffffffu, (needA || needB) && j > 0)) {
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      sm.rwA[m] = rwA[m];
-      sm.rwB[m] = rwB[m];
-    }
-    sm.rh_park = rh_park;
-    sm.prowA = prowA;
-    sm.prowB = prowB;
-    sm.bars = bars;
-    sm.q = q;
-    sm.lane = lane;
-    sm.oA = out + (bh * kN + row0 + prowA) * HD + 2 * c;
-    sm.abort_flag = abort_flag;
-    if constexpr (!kBf16) {
-      if (okk) sm.exact_pass(0);
+        for (int c0 = 0; c0 < L::kOCols; c0 += 16) {
+          uint32_t ov[8];
+          tmem_ld_16x256b_x2(tO + c0, ov);
+          tmem_wait_ld_regs(ov);
+          ov[0] = __float_as_uint(__uint_as_float(ov[0]) * alA);
+          ov[1] = __float_as_uint(__uint_as_float(ov[1]) * alA);
+          ov[4] = __float_as_uint(__uint_as_float(ov[4]) * alA);
+          ov[5] = __float_as_uint(__uint_as_float(ov[5]) * alA);
+          ov[2] = __float_as_uint(__uint_as_float(ov[2]) * alB);
+          ov[3] = __float_as_uint(__uint_as_float(ov[3]) * alB);
+          ov[6] = __float_as_uint(__uint_as_float(ov[6]) * alB);
+          ov[7] = __float_as_uint(__uint_as_float(ov[7]) * alB);
+          tmem_st_16x256b_x2(tO + c0, ov);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[q]);
+    };
+    // Epilogue of a pass: O / l -> out once PV_q of the last tile has completed; false if an output is not
+    // finite.
+    auto epilogue = [&](int pass) {
+      bool finite = true;
+      if (okk) okk = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[q], pass & 1, abort_flag));
+      if (okk) {
+        tc_fence_after();
+        // every column of the ones block holds the row sum
+        uint32_t lv[8];
+        tmem_ld_16x256b_x2(tO + HD, lv);
+        tmem_wait_ld_regs(lv);
+        const float invA = 1.f / __uint_as_float(lv[0]), invB = 1.f / __uint_as_float(lv[2]);
+        T* oA = out + (bh * kN + row0 + prowA) * HD + 2 * c;
+        T* oB = oA + 8 * HD;
+#pragma unroll
+        for (int c0 = 0; c0 < HD; c0 += 16) {
+          uint32_t ov[8];
+          tmem_ld_16x256b_x2(tO + c0, ov);
+          tmem_wait_ld_regs(ov);
+          float y[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            y[e] = __uint_as_float(ov[e]) * ((e & 2) ? invB : invA);
+            finite &= fabsf(y[e]) < INFINITY;  // false for inf and NaN
+          }
+          *reinterpret_cast<uint32_t*>(oA + c0) = pack2(y[0], y[1], kBf16);
+          *reinterpret_cast<uint32_t*>(oA + c0 + 8) = pack2(y[4], y[5], kBf16);
+          *reinterpret_cast<uint32_t*>(oB + c0) = pack2(y[2], y[3], kBf16);
+          *reinterpret_cast<uint32_t*>(oB + c0 + 8) = pack2(y[6], y[7], kBf16);
+        }
+      }
+      return finite;
+    };
+    // The exact two-pass softmax over all key tiles (f16, and the marked CTAs of the bf16 fixup launch).
+    auto exact_pass = [&](int pass) {
+      mrA = -INFINITY;
+      mrB = -INFINITY;
+      for (int j = 0; j < kNT && okk; ++j) {
+        okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
+        if (!okk) break;
+        tc_fence_after();
+        const float rhA0 = rh_park[(2 * j) * 256 + prowA], rhA1 = rh_park[(2 * j + 1) * 256 + prowA];
+        const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
+        bool needA, needB;
+        float alA = 1.f, alB = 1.f, tA, tB;
+        exact_tile(j, rhA0, rhA1, rhB0, rhB1, alA, alB, needA, needB, tA, tB, nullptr, nullptr);
+        finish_tile(j, needA, needB, alA, alB);
+      }
+      epilogue(pass);
+    };
+    if constexpr (MODE != kModeSpec) {
+      exact_pass(0);
     } else {
       // Speculative pass (bf16): the first tile exact, the others in a single pass. Per row: run = the
       // running max of the full score, base = that of S*c + rw (without the per-key-row rh term), rhmax =
       // the largest rh over all key rows. base + rhmax bounds a tile's max unless the base grows within it;
       // the prediction is that bound capped kSpecCap above run, and the reference is raised to it once it
       // passes the reference by kSpecRaise. Any reference gives the same softmax (O and its row sums scale
-      // together), and bf16 P and the f32 sums hold 2^-126 .. 2^127: the exponents are tracked, and if one
-      // exceeds kSpecLimit or an output is not finite, the CTA runs the exact pass.
+      // together) and bf16 P and the f32 sums hold 2^-126 .. 2^127: the exponents are tracked, and if one
+      // exceeds kSpecLimit or an output is not finite, the CTA leaves the NaN marker for the fixup launch.
       float runA, runB, baseA, baseB, rhmaxA = -INFINITY, rhmaxB = -INFINITY;
       bool unsafe = false;
-      sm.mrA = -INFINITY;
-      sm.mrB = -INFINITY;
       for (int j = 0; j < kNT && okk; ++j) {
         okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
         if (!okk) break;
         tc_fence_after();
-        const float rhA0 = sm.rh(2 * j, prowA), rhA1 = sm.rh(2 * j + 1, prowA);
-        const float rhB0 = sm.rh(2 * j, prowB), rhB1 = sm.rh(2 * j + 1, prowB);
+        const float rhA0 = rh_park[(2 * j) * 256 + prowA], rhA1 = rh_park[(2 * j + 1) * 256 + prowA];
+        const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
         bool needA, needB;
         float alA = 1.f, alB = 1.f;
         if (j == 0) {
 #pragma unroll 8
           for (int kh = 0; kh < 64; ++kh) {
-            rhmaxA = fmaxf(rhmaxA, sm.rh(kh, prowA));
-            rhmaxB = fmaxf(rhmaxB, sm.rh(kh, prowB));
+            rhmaxA = fmaxf(rhmaxA, rh_park[kh * 256 + prowA]);
+            rhmaxB = fmaxf(rhmaxB, rh_park[kh * 256 + prowB]);
           }
-          sm.template exact_tile<true>(j, rhA0, rhA1, rhB0, rhB1, alA, alB, needA, needB, runA, runB, baseA,
-                                       baseB);
+          exact_tile(j, rhA0, rhA1, rhB0, rhB1, alA, alB, needA, needB, runA, runB, &baseA, &baseB);
         } else {
           const float pA = fminf(baseA + rhmaxA, runA + kSpecCap), pB = fminf(baseB + rhmaxB, runB + kSpecCap);
-          needA = pA > sm.mrA + kSpecRaise;
-          needB = pB > sm.mrB + kSpecRaise;
+          needA = pA > mrA + kSpecRaise;
+          needB = pB > mrB + kSpecRaise;
           if (needA) {
-            alA = ex2(sm.mrA - pA);
-            sm.mrA = pA;
+            alA = ex2(mrA - pA);
+            mrA = pA;
           }
           if (needB) {
-            alB = ex2(sm.mrB - pB);
-            sm.mrB = pB;
+            alB = ex2(mrB - pB);
+            mrB = pB;
           }
           float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-          sm.template pass2<true>(rhA0, rhA1, rhB0, rhB1, xm);
+          pass2(std::integral_constant<bool, true>{}, rhA0, rhA1, rhB0, rhB1, xm);
           unsafe |= fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])) > kSpecLimit;
           // the tile's base and max: the exponent maxima + m (- rh), across the row's four threads
-          float bA = fmaxf(xm[0] - rhA0, xm[1] - rhA1) + sm.mrA, bB = fmaxf(xm[2] - rhB0, xm[3] - rhB1) + sm.mrB;
-          float uA = fmaxf(xm[0], xm[1]) + sm.mrA, uB = fmaxf(xm[2], xm[3]) + sm.mrB;
+          float bA = fmaxf(xm[0] - rhA0, xm[1] - rhA1) + mrA, bB = fmaxf(xm[2] - rhB0, xm[3] - rhB1) + mrB;
+          float uA = fmaxf(xm[0], xm[1]) + mrA, uB = fmaxf(xm[2], xm[3]) + mrB;
           bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 1));
           bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 1));
           uA = fmaxf(uA, __shfl_xor_sync(0xffffffffu, uA, 1));
@@ -773,12 +712,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           runA = fmaxf(runA, uA);
           runB = fmaxf(runB, uB);
         }
-        sm.finish_tile(j, needA, needB, alA, alB);
+        finish_tile(j, needA, needB, alA, alB);
       }
-      bool finite = true;
-      if (okk) okk = sm.epilogue(0, finite);
-      if (__any_sync(0xffffffffu, unsafe || !finite) && lane == 0) bars->rerun = 1;
-      if (rerun_pass()) softmax_rerun<T, HD>(sm);
+      unsafe |= !epilogue(0);
+      // The marker goes in after its element's own output (written by this very thread of warp 4 in its
+      // epilogue) and after every warp's flag.
+      if (__any_sync(0xffffffffu, unsafe) && lane == 0) bars->rerun = 1;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->epi_done);
+      if (warp == 4 && __all_sync(0xffffffffu, mbar_wait(&bars->epi_done, 0, abort_flag)) && lane == 0 &&
+          *reinterpret_cast<volatile int*>(&bars->rerun) != 0)
+        *marker = from_f<T>(__int_as_float(0x7fc00000));
     }
   }
   tc_fence_before();
