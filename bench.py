@@ -344,6 +344,8 @@ def run_ours(args):
     roofs = {k: roof(k) for k in ("global", "window")}
     dominant = max(roofs, key=lambda k: roofs[k]["time_share"])
 
+    neighbours = run_neighbours(samrs, lib, images, device, sptr, hbm) if not args.no_neighbours else None
+
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world)
@@ -378,11 +380,57 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if e2e is not None:
             line["e2e"] = e2e
+        if neighbours is not None:
+            line["neighbours"] = neighbours
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def run_neighbours(samrs, lib, images, device, sptr, hbm, reps=10):
+    """The path's neighbours on the token grid at the bench workload (not part of the metric): the qkv
+    split fused with the window partition and the head merge fused with the unpartition, for the windowed
+    (ws 14, pad 64 -> 70) and the global (one 64x64 window) layers. Algorithmic bytes: the real tokens'
+    y (3C) read and q, kt, v (pads included) written; the real tokens' attention rows read and written."""
+    import torch
+    nh, c, es = 16, 16 * HD, 2
+    out = {}
+    y = (torch.randn(images * 4096, 3 * c, device=device) * 0.5).to(torch.bfloat16)
+    bias = (torch.randn(3 * c, device=device) * 0.1).to(torch.bfloat16)
+    for name, ws in (("window", 14), ("global", 0)):
+        n, nwin = (196, 25) if ws else (4096, 1)
+        bh = images * nwin * nh
+        packed = torch.empty(3 * bh * n * HD, device=device, dtype=torch.bfloat16)
+        attn = torch.empty(bh, n, HD, device=device, dtype=torch.bfloat16)
+        merged = torch.empty(images * 4096, c, device=device, dtype=torch.bfloat16)
+        calls = {
+            "qkv_split_window": (lambda: lib.samrs_qkv_split_window_fwd(
+                y.data_ptr(), bias.data_ptr(), packed.data_ptr(), images, 64, 64, ws, nh, HD, 2, sptr),
+                images * 4096 * 3 * c * es + 3 * bh * n * HD * es),
+            "window_merge": (lambda: lib.samrs_window_merge_fwd(
+                attn.data_ptr(), merged.data_ptr(), images, 64, 64, ws, nh, HD, 2, sptr),
+                2 * images * 4096 * c * es),
+        }
+        for kname, (fn, nbytes) in calls.items():
+            for _ in range(3):
+                if fn() != 0:
+                    raise RuntimeError(lib.samrs_last_error().decode())
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(reps):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / reps
+            gbs = nbytes / (ms / 1e3) / 1e9
+            out[f"{kname} ({name})"] = {"ms": ms, "GB/s": gbs, "frac_of_hbm": gbs / hbm, "bytes": nbytes}
+        del packed, attn, merged
+    if samrs.device_status() != 0:
+        raise RuntimeError("device status word set by the neighbour kernels")
+    return out
 
 
 def run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world):
@@ -483,6 +531,7 @@ def main(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-neighbours", action="store_true", help="skip timing the qkv split / head merge kernels")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

@@ -11,6 +11,10 @@
  *                               and its CUDA launcher src/kernels.rs:1108-1149 (kernels/sam.cu:44-106)
  *   samrs_qkv_split_fwd      <- src/kernels.rs:870-894 `qkv_split(y, bias, n, nh, hd)`
  *                               and its CUDA launcher src/kernels.rs:1196-1227 (kernels/sam.cu:108-128)
+ *   samrs_qkv_split_window_fwd <- src/sam1/encoder.rs:132-140 `window_partition` (zero pad) followed
+ *                               by the qkv projection's bias and `qkv_split` (src/kernels.rs:870-894)
+ *   samrs_window_merge_fwd   <- src/sam1/encoder.rs:82 (heads back to [windows * n, C]) followed by
+ *                               `window_unpartition` (src/sam1/encoder.rs:142-145, crop)
  *
  * Conventions shared by every entry point
  *  - All tensors are dense, contiguous, row-major device buffers owned by the caller
@@ -97,6 +101,26 @@ SAMRS_API int samrs_relpos_softmax_fwd(const void* s, const void* q, const void*
  */
 SAMRS_API int samrs_qkv_split_fwd(const void* y, const void* bias, void* out, int64_t tokens, int n, int nh, int hd,
                         int dtype, void* stream);
+
+/*
+ * QKV head split fused with the window partition (the neighbours of the attention on the token grid):
+ *   y [images*h*w, 3*nh*hd] (the qkv projection of the REAL tokens, without bias) + bias [3*nh*hd]
+ *   -> out = [q | kt | v], q, v: [bh, n, hd], kt: [bh, hd, n], bh = window * nh + head,
+ *   n = ws*ws, windows row-major per image over the grid zero-padded up to multiples of ws
+ *   (window_partition's order). A pad token's q/k/v is the bias alone: in the reference its input is
+ *   zero, so its projection is 0 * W + bias. ws = 0: one window of h x w (the global layers; no pad),
+ *   which is `qkv_split` on the token grid.
+ */
+SAMRS_API int samrs_qkv_split_window_fwd(const void* y, const void* bias, void* out, int64_t images, int h, int w,
+                                         int ws, int nh, int hd, int dtype, void* stream);
+
+/*
+ * Head merge fused with the window unpartition: attn [bh, n, hd] (layout as above) -> out [images*h*w,
+ * nh*hd], the real tokens only (the pads are cropped). The output projection, a per-token GEMM, then
+ * runs on the real tokens, which gives the same rows as the reference's projection before the crop.
+ */
+SAMRS_API int samrs_window_merge_fwd(const void* attn, void* out, int64_t images, int h, int w, int ws, int nh, int hd,
+                                     int dtype, void* stream);
 
 /* Message describing the last error returned on the calling thread ("" if none). */
 SAMRS_API const char* samrs_last_error(void);

@@ -96,3 +96,55 @@ def qkv_split(y, bias, n, nh, hd):
     plane = tokens * nh * hd
     return (out[:plane].reshape(bh, n, hd), out[plane:2 * plane].reshape(bh, hd, n),
             out[2 * plane:].reshape(bh, n, hd))
+
+
+def window_partition(x, ws):
+    """[B, H, W, C] -> [B * nWh * nWw, ws, ws, C], zero-padding H and W up to multiples of ws
+    (src/sam1/encoder.rs:132-140: pad, reshape [B, Hp/ws, ws, Wp/ws, ws, C], swap the two middle axes)."""
+    x = np.asarray(x)
+    b, h, w, c = x.shape
+    hp, wp = -(-h // ws) * ws, -(-w // ws) * ws
+    xp = np.zeros((b, hp, wp, c), x.dtype)
+    xp[:, :h, :w] = x
+    xp = xp.reshape(b, hp // ws, ws, wp // ws, ws, c).transpose(0, 1, 3, 2, 4, 5)
+    return xp.reshape(-1, ws, ws, c)
+
+
+def window_unpartition(xw, ws, h, w):
+    """Inverse of window_partition, cropping the pads (src/sam1/encoder.rs:142-145): [B*nW, ws, ws, C] ->
+    [B, H, W, C]."""
+    xw = np.asarray(xw)
+    c = xw.shape[-1]
+    hp, wp = -(-h // ws) * ws, -(-w // ws) * ws
+    b = xw.shape[0] // ((hp // ws) * (wp // ws))
+    x = xw.reshape(b, hp // ws, wp // ws, ws, ws, c).transpose(0, 1, 3, 2, 4, 5).reshape(b, hp, wp, c)
+    return x[:, :h, :w]
+
+
+def qkv_split_window(y, bias, images, h, w, ws, nh, hd):
+    """The reference's order for the windowed input side: the qkv projection y of the real tokens
+    [images*h*w, 3C] (no bias) is laid on the token grid, window_partition pads with zero projections
+    (a zero input token projects to 0), then qkv_split adds the bias and splits heads
+    (src/sam1/encoder.rs:132-140, src/kernels.rs:234-263). ws = 0: one window of h x w."""
+    y = _f32(y)
+    c3 = y.shape[1]
+    grid = y.reshape(images, h, w, c3)
+    if ws:
+        win = window_partition(grid, ws)
+        n = ws * ws
+    else:
+        win, n = grid, h * w
+    return qkv_split(np.ascontiguousarray(win.reshape(-1, c3)), bias, n, nh, hd)
+
+
+def window_merge(attn, images, h, w, ws, nh, hd):
+    """attn [bh, n, hd] -> heads back to [windows, n, C] (src/sam1/encoder.rs:82) -> window_unpartition crop
+    (:142-145) -> [images*h*w, C]. ws = 0: one window of h x w."""
+    attn = _f32(attn)
+    bh, n, _ = attn.shape
+    tok = attn.reshape(bh // nh, nh, n, hd).transpose(0, 2, 1, 3).reshape(bh // nh, n, nh * hd)
+    if ws:
+        grid = window_unpartition(tok.reshape(-1, ws, ws, nh * hd), ws, h, w)
+    else:
+        grid = tok.reshape(images, h, w, nh * hd)
+    return np.ascontiguousarray(grid.reshape(images * h * w, nh * hd))

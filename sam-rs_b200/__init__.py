@@ -21,8 +21,9 @@ import torch
 from . import _abi
 from ._abi import SamrsError
 
-__all__ = ["relpos_softmax", "attention_relpos", "attention_relpos_cpu", "qkv_split", "bmm", "Attention",
-           "window_partition", "window_unpartition", "device_status", "SamrsError"]
+__all__ = ["relpos_softmax", "attention_relpos", "attention_relpos_cpu", "qkv_split", "qkv_split_window",
+           "window_merge", "bmm", "Attention", "window_partition", "window_unpartition", "device_status",
+           "SamrsError"]
 
 _DTYPES = {torch.float32: _abi.F32, torch.float16: _abi.F16, torch.bfloat16: _abi.BF16}
 _IMPLS = {"auto": _abi.IMPL_AUTO, "simt": _abi.IMPL_SIMT, "tc": _abi.IMPL_TC}
@@ -115,6 +116,43 @@ def qkv_split(y, bias, n, nh, hd):
     plane = t * nh * hd
     return (packed[:plane].view(bh, n, hd), packed[plane:2 * plane].view(bh, hd, n),
             packed[2 * plane:].view(bh, n, hd))
+
+
+def _win_counts(h, w, ws):
+    wh, ww = (ws, ws) if ws else (h, w)
+    return wh * ww, ((h + wh - 1) // wh) * ((w + ww - 1) // ww)
+
+
+def qkv_split_window(y, bias, images, h, w, ws, nh, hd):
+    """window_partition (zero pad, src/sam1/encoder.rs:132-140) + qkv bias + qkv_split (src/kernels.rs:870-894)
+    in one pass: y [images*h*w, 3*nh*hd] is the projection of the real tokens (no bias); returns
+    (q [BH,n,hd], kt [BH,hd,n], v [BH,n,hd]), BH = images * windows * nh, n = ws*ws; pad tokens get the bias.
+    ws = 0: one window of h x w (global layers)."""
+    code = _dtype_code(y, bias)
+    c = nh * hd
+    if y.dim() != 2 or y.shape[0] != images * h * w or y.shape[1] != 3 * c or bias.numel() != 3 * c:
+        raise SamrsError(_abi.ERR_INVALID, "qkv_split_window: shape mismatch")
+    n, nwin = _win_counts(h, w, ws)
+    bh = images * nwin * nh
+    packed = torch.empty(3 * bh * n * hd, dtype=y.dtype, device=y.device)
+    _abi.check(_abi.lib().samrs_qkv_split_window_fwd(y.data_ptr(), bias.data_ptr(), packed.data_ptr(), images, h, w,
+                                                     ws, nh, hd, code, _stream()))
+    plane = bh * n * hd
+    return (packed[:plane].view(bh, n, hd), packed[plane:2 * plane].view(bh, hd, n),
+            packed[2 * plane:].view(bh, n, hd))
+
+
+def window_merge(attn, images, h, w, ws, nh, hd):
+    """Heads back to tokens (src/sam1/encoder.rs:82) + window_unpartition crop (:142-145): attn [BH, n, hd] ->
+    [images*h*w, nh*hd], the real tokens only."""
+    code = _dtype_code(attn)
+    n, nwin = _win_counts(h, w, ws)
+    if attn.shape != (images * nwin * nh, n, hd) or not attn.is_contiguous():
+        raise SamrsError(_abi.ERR_INVALID, "window_merge: shape mismatch")
+    out = torch.empty(images * h * w, nh * hd, dtype=attn.dtype, device=attn.device)
+    _abi.check(_abi.lib().samrs_window_merge_fwd(attn.data_ptr(), out.data_ptr(), images, h, w, ws, nh, hd, code,
+                                                 _stream()))
+    return out
 
 
 def bmm(a, b):

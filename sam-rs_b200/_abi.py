@@ -44,10 +44,13 @@ def lib():
         l.samrs_relpos_attn_fwd_ex.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, f32, i32, i32, vp]
         l.samrs_relpos_softmax_fwd.argtypes = [vp, vp, vp, vp, i64, i32, i32, i32, f32, i32, vp]
         l.samrs_qkv_split_fwd.argtypes = [vp, vp, vp, i64, i32, i32, i32, i32, vp]
+        l.samrs_qkv_split_window_fwd.argtypes = [vp, vp, vp, i64, i32, i32, i32, i32, i32, i32, vp]
+        l.samrs_window_merge_fwd.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, i32, vp]
         l.samrs_last_error.restype = ctypes.c_char_p
         l.samrs_device_status.argtypes = [vp, i32]
         for name in ("samrs_relpos_attn_fwd", "samrs_relpos_attn_fwd_ex", "samrs_relpos_softmax_fwd",
-                     "samrs_qkv_split_fwd", "samrs_abi_version", "samrs_device_status"):
+                     "samrs_qkv_split_fwd", "samrs_qkv_split_window_fwd", "samrs_window_merge_fwd",
+                     "samrs_abi_version", "samrs_device_status"):
             getattr(l, name).restype = i32
         _lib = l
     return _lib

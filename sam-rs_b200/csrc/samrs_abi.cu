@@ -3,6 +3,8 @@
 // caller-owned device buffers, enqueue on the caller's stream, allocate nothing and never synchronise.
 #include <cuda_runtime.h>
 #include <stdarg.h>
+
+#include <algorithm>
 #include <stdint.h>
 #include <stdio.h>
 
@@ -10,6 +12,7 @@
 #include "common.cuh"
 #include "relpos_simt.cuh"
 #include "relpos_tc.cuh"
+#include "window_io.cuh"
 
 namespace {
 
@@ -122,6 +125,60 @@ int launch_split(const void* y, const void* bias, void* out, int64_t tokens, int
   return launch_status("qkv_split");
 }
 
+bool aligned16_all(const void* a, const void* b, const void* c) {
+  return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c)) & 15u) == 0;
+}
+
+// Window geometry of a (images, h, w, ws) call; ws = 0: one window of h x w.
+int win_geom(const char* what, int64_t images, int h, int w, int ws, int nh, int hd, WinGeom* g) {
+  if (images < 0 || h < 1 || w < 1 || ws < 0 || nh < 1 || hd < 1 || hd > 1024 || h > 65535 || w > 65535 ||
+      ws > 65535)
+    return fail(SAMRS_ERR_INVALID, "%s: bad geometry images=%lld h=%d w=%d ws=%d nh=%d hd=%d", what, (long long)images,
+                h, w, ws, nh, hd);
+  g->h = h;
+  g->w = w;
+  g->wh = ws ? ws : h;
+  g->ww = ws ? ws : w;
+  g->nwh = (h + g->wh - 1) / g->wh;
+  g->nww = (w + g->ww - 1) / g->ww;
+  g->nh = nh;
+  g->hd = hd;
+  if ((int64_t)g->wh * g->ww > (1 << 24)) return fail(SAMRS_ERR_UNSUPPORTED, "%s: window too large", what);
+  return ok();
+}
+
+template <typename T>
+int launch_split_window(const void* y, const void* bias, void* out, int64_t images, const WinGeom& g, cudaStream_t st) {
+  const int64_t units = images * g.nwh * g.nww * g.nh;
+  const int gy = (g.n() + kWinTok - 1) / kWinTok;
+  if (units > 0x7fffffffLL || gy > 65535) return fail(SAMRS_ERR_UNSUPPORTED, "qkv_split_window: grid too large");
+  const size_t smem = (size_t)kWinTok * (g.hd + 1) * sizeof(float);
+  constexpr int kVec = 16 / (int)sizeof(T);
+  const dim3 grid((unsigned)units, gy);
+  if ((g.hd * (int)sizeof(T)) % 16 == 0 && aligned16_all(y, bias, out))
+    qkv_split_window_kernel<T, kVec><<<grid, 256, smem, st>>>(static_cast<const T*>(y), static_cast<const T*>(bias),
+                                                               static_cast<T*>(out), (long)units, g);
+  else
+    qkv_split_window_kernel<T, 1><<<grid, 256, smem, st>>>(static_cast<const T*>(y), static_cast<const T*>(bias),
+                                                            static_cast<T*>(out), (long)units, g);
+  return launch_status("qkv_split_window");
+}
+
+template <typename T>
+int launch_merge(const void* attn, void* out, int64_t images, const WinGeom& g, int num_sms, cudaStream_t st) {
+  constexpr int kVec = 16 / (int)sizeof(T);
+  const bool vec = (g.hd * (int)sizeof(T)) % 16 == 0 && aligned16_all(attn, out, out);
+  const int64_t chunks = images * g.h * (int64_t)g.w * g.c() / (vec ? kVec : 1);
+  const int64_t blocks = std::min<int64_t>((chunks + 255) / 256, (int64_t)num_sms * 16);
+  if (vec)
+    window_merge_kernel<T, kVec><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const T*>(attn), static_cast<T*>(out),
+                                                                   (long)images, g);
+  else
+    window_merge_kernel<T, 1><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const T*>(attn), static_cast<T*>(out),
+                                                                (long)images, g);
+  return launch_status("window_merge");
+}
+
 }  // namespace
 
 extern "C" {
@@ -219,6 +276,52 @@ int samrs_qkv_split_fwd(const void* y, const void* bias, void* out, int64_t toke
       return launch_split<__half>(y, bias, out, tokens, n, nh, hd, st);
     default:
       return launch_split<__nv_bfloat16>(y, bias, out, tokens, n, nh, hd, st);
+  }
+}
+
+int samrs_qkv_split_window_fwd(const void* y, const void* bias, void* out, int64_t images, int h, int w, int ws, int nh,
+                               int hd, int dtype, void* stream) {
+  if (dtype != SAMRS_F32 && dtype != SAMRS_F16 && dtype != SAMRS_BF16)
+    return fail(SAMRS_ERR_INVALID, "qkv_split_window: unsupported dtype code %d", dtype);
+  WinGeom g;
+  int rc = win_geom("qkv_split_window", images, h, w, ws, nh, hd, &g);
+  if (rc) return rc;
+  if (images == 0) return ok();
+  if (!y || !bias || !out) return fail(SAMRS_ERR_INVALID, "qkv_split_window: null pointer");
+  DevInfo* dev = nullptr;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SAMRS_F32:
+      return launch_split_window<float>(y, bias, out, images, g, st);
+    case SAMRS_F16:
+      return launch_split_window<__half>(y, bias, out, images, g, st);
+    default:
+      return launch_split_window<__nv_bfloat16>(y, bias, out, images, g, st);
+  }
+}
+
+int samrs_window_merge_fwd(const void* attn, void* out, int64_t images, int h, int w, int ws, int nh, int hd, int dtype,
+                           void* stream) {
+  if (dtype != SAMRS_F32 && dtype != SAMRS_F16 && dtype != SAMRS_BF16)
+    return fail(SAMRS_ERR_INVALID, "window_merge: unsupported dtype code %d", dtype);
+  WinGeom g;
+  int rc = win_geom("window_merge", images, h, w, ws, nh, hd, &g);
+  if (rc) return rc;
+  if (images == 0) return ok();
+  if (!attn || !out) return fail(SAMRS_ERR_INVALID, "window_merge: null pointer");
+  DevInfo* dev = nullptr;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SAMRS_F32:
+      return launch_merge<float>(attn, out, images, g, dev->num_sms, st);
+    case SAMRS_F16:
+      return launch_merge<__half>(attn, out, images, g, dev->num_sms, st);
+    default:
+      return launch_merge<__nv_bfloat16>(attn, out, images, g, dev->num_sms, st);
   }
 }
 

@@ -15,7 +15,8 @@ def test_library_exports_every_header_symbol():
     a = abi()
     names = a.header_symbols()
     assert set(names) >= {"samrs_relpos_attn_fwd", "samrs_relpos_attn_fwd_ex", "samrs_relpos_softmax_fwd",
-                          "samrs_qkv_split_fwd", "samrs_last_error", "samrs_abi_version", "samrs_device_status"}
+                          "samrs_qkv_split_fwd", "samrs_qkv_split_window_fwd", "samrs_window_merge_fwd",
+                          "samrs_last_error", "samrs_abi_version", "samrs_device_status"}
     lib = ctypes.CDLL(a.LIB_PATH)
     for n in names:
         assert hasattr(lib, n), n
@@ -72,3 +73,23 @@ def test_host_mirror_rejects_cpu_tensors():
     with pytest.raises(s.SamrsError):
         s.attention_relpos(q, kt, q, t, 4, 4, 0.5)
     assert s.attention_relpos_cpu(q, kt, q, t, 4, 4, 0.5) is None
+
+
+@pytest.mark.parametrize("args", [dict(dtype=5), dict(images=-1), dict(h=0), dict(ws=-1), dict(nh=0), dict(hd=0)])
+def test_window_io_rejects_bad_arguments(args):
+    a = abi()
+    p = dict(images=1, h=8, w=8, ws=4, nh=2, hd=8, dtype=2)
+    p.update(args)
+    rc = a.lib().samrs_qkv_split_window_fwd(0, 0, 0, p["images"], p["h"], p["w"], p["ws"], p["nh"], p["hd"],
+                                            p["dtype"], None)
+    assert rc == -1 and a.lib().samrs_last_error()
+    rc = a.lib().samrs_window_merge_fwd(0, 0, p["images"], p["h"], p["w"], p["ws"], p["nh"], p["hd"], p["dtype"], None)
+    assert rc == -1 and a.lib().samrs_last_error()
+
+
+def test_window_io_empty_and_null():
+    a = abi()
+    assert a.lib().samrs_qkv_split_window_fwd(0, 0, 0, 0, 64, 64, 14, 16, 80, 2, None) == 0
+    assert a.lib().samrs_window_merge_fwd(0, 0, 0, 64, 64, 14, 16, 80, 2, None) == 0
+    assert a.lib().samrs_qkv_split_window_fwd(0, 0, 0, 1, 64, 64, 14, 16, 80, 2, None) == -1
+    assert a.lib().samrs_window_merge_fwd(0, 0, 1, 64, 64, 14, 16, 80, 2, None) == -1

@@ -237,6 +237,65 @@ def test_attention_block_chain(samrs, cuda):
     assert rel_max_err(y.reshape(-1, c).cpu().numpy(), ref.numpy()) < 1e-3
 
 
+WIN_GEOMS = [(2, 64, 64, 14, 16, 80), (2, 13, 20, 7, 3, 24), (1, 16, 16, 0, 4, 32), (1, 14, 14, 14, 2, 16),
+             (1, 9, 11, 4, 2, 12)]
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("images,h,w,ws,nh,hd", WIN_GEOMS)
+def test_qkv_split_window_matches_oracle(samrs, cuda, images, h, w, ws, nh, hd, dt):
+    """window_partition (zero pad) + qkv bias + qkv_split in one kernel, bit-exact against the oracle's
+    restatement of the reference order (src/sam1/encoder.rs:132-140, src/kernels.rs:234-263)."""
+    rng = np.random.default_rng(h * 31 + w + hd)
+    c = nh * hd
+    y = rng.standard_normal((images * h * w, 3 * c), dtype=np.float32)
+    b = rng.standard_normal(3 * c, dtype=np.float32)
+    yd, bd = to_dev(y, dt, cuda), to_dev(b, dt, cuda)
+    got = samrs.qkv_split_window(yd, bd, images, h, w, ws, nh, hd)
+    want = oracle.qkv_split_window(rounded(yd), rounded(bd), images, h, w, ws, nh, hd)
+    for g_, w_ in zip(got, want):
+        ref = torch.from_numpy(np.ascontiguousarray(w_)).to(DT[dt]).float().numpy()  # one rounding of the sum
+        assert g_.shape == w_.shape
+        assert np.array_equal(g_.float().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+@pytest.mark.parametrize("images,h,w,ws,nh,hd", WIN_GEOMS)
+def test_window_merge_matches_oracle(samrs, cuda, images, h, w, ws, nh, hd, dt):
+    """Heads back to tokens + window_unpartition crop (src/sam1/encoder.rs:82,142-145), bit-exact."""
+    wh, ww = (ws, ws) if ws else (h, w)
+    bh = images * (-(-h // wh)) * (-(-w // ww)) * nh
+    a = np.random.default_rng(h + w).standard_normal((bh, wh * ww, hd), dtype=np.float32)
+    ad = to_dev(a, dt, cuda)
+    got = samrs.window_merge(ad, images, h, w, ws, nh, hd)
+    want = oracle.window_merge(rounded(ad), images, h, w, ws, nh, hd)
+    assert np.array_equal(got.float().cpu().numpy(), want)
+
+
+def test_windowed_block_fused_io_chain(samrs, cuda):
+    """The windowed ViT-B block on the real tokens only: qkv GEMM on the 64x64 grid -> qkv_split_window ->
+    fused attention -> window_merge -> proj, against the reference order (window_partition with zero pad ->
+    qkv GEMM on all 70x70 tokens -> qkv_split -> attention -> proj -> window_unpartition) with the oracle
+    for the attention."""
+    torch.manual_seed(5)
+    c, nh, hd = 768, 12, 64
+    x = torch.randn(1, 64, 64, c, device=cuda)
+    att = samrs.Attention(torch.randn(3 * c, c, device=cuda) * 0.02, torch.randn(3 * c, device=cuda) * 0.02,
+                          torch.randn(c, c, device=cuda) * 0.02, torch.zeros(c, device=cuda),
+                          torch.randn(27, 64, device=cuda) * 0.5, torch.randn(27, 64, device=cuda) * 0.5, nh)
+    y = (x.reshape(-1, c) @ att.qkv_wt).contiguous()
+    q, kt, v = samrs.qkv_split_window(y, att.qkv_b, 1, 64, 64, 14, nh, hd)
+    ctx = samrs.attention_relpos(q, kt, v, att.rel, 14, 14, att.scale)
+    got = samrs.window_merge(ctx, 1, 64, 64, 14, nh, hd) @ att.proj_wt
+    parts = oracle.window_partition(x.cpu().numpy(), 14)
+    qkv = parts.reshape(-1, c) @ att.qkv_wt.cpu().numpy()
+    q2, kt2, v2 = oracle.qkv_split(qkv, att.qkv_b.cpu().numpy(), 196, nh, hd)
+    ctx2 = oracle.attention_relpos(q2, kt2, v2, att.rel.cpu().numpy(), 14, 14, hd ** -0.5)
+    tok = ctx2.reshape(25, nh, 196, hd).transpose(0, 2, 1, 3).reshape(-1, c) @ att.proj_wt.cpu().numpy()
+    ref = oracle.window_unpartition(tok.reshape(25, 14, 14, c), 14, 64, 64).reshape(-1, c)
+    assert rel_max_err(got.cpu().numpy(), ref) < 1e-3
+
+
 def test_empty_and_status(samrs, cuda):
     q = torch.zeros(0, 16, 8, device=cuda)
     out = samrs.attention_relpos(q, torch.zeros(0, 8, 16, device=cuda), q, torch.zeros(14, 8, device=cuda), 4, 4, 1.0)

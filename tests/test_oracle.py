@@ -76,3 +76,37 @@ def test_ragged_shapes_match_float64(h, w, bh, hd):
 def test_empty_batch():
     q, kt, v, t = make_rand(4, 4, 0, 8, seed=1)
     assert oracle.attention_relpos(q, kt, v, t, 4, 4, 0.5).shape == (0, 16, 8)
+
+
+@pytest.mark.parametrize("b,h,w,ws", [(2, 64, 64, 14), (1, 13, 20, 7), (3, 14, 14, 14)])
+def test_window_partition_matches_package_mirror(b, h, w, ws):
+    """The oracle's numpy window_partition / window_unpartition (src/sam1/encoder.rs:132-145) against the
+    package's torch mirror (the layout the model code uses), both ways."""
+    import torch
+    from tests.conftest import load_samrs
+    s = load_samrs()
+    x = np.random.default_rng(b + h + w).standard_normal((b, h, w, 5), dtype=np.float32)
+    parts = oracle.window_partition(x, ws)
+    tparts, hp, wp = s.window_partition(torch.from_numpy(x), ws)
+    assert np.array_equal(parts, tparts.numpy())
+    assert np.array_equal(oracle.window_unpartition(parts, ws, h, w), x)
+    back = s.window_unpartition(tparts, ws, hp, wp, (h, w), b, 5)
+    assert np.array_equal(back.numpy(), x)
+
+
+@pytest.mark.parametrize("images,h,w,ws,nh,hd", [(2, 13, 20, 7, 3, 8), (1, 16, 16, 0, 2, 8)])
+def test_window_merge_inverts_split(images, h, w, ws, nh, hd):
+    """window_merge(q of qkv_split_window) is y_q + b_q on the real tokens; pad tokens hold the bias."""
+    rng = np.random.default_rng(images * 7 + h)
+    c = nh * hd
+    y = rng.standard_normal((images * h * w, 3 * c), dtype=np.float32)
+    b = rng.standard_normal(3 * c, dtype=np.float32)
+    q, kt, v = oracle.qkv_split_window(y, b, images, h, w, ws, nh, hd)
+    assert np.array_equal(oracle.window_merge(q, images, h, w, ws, nh, hd), y[:, :c] + b[:c])
+    assert np.array_equal(oracle.window_merge(v, images, h, w, ws, nh, hd), y[:, 2 * c:] + b[2 * c:])
+    if ws:
+        # the last window of image 0 starts in the grid and runs past it: its pad tokens are the bias
+        nww = -(-w // ws)
+        last = (nww - 1) * nh  # window (0, nww-1), head 0
+        tok_pad = ws - 1  # column (nww-1)*ws + ws-1 >= w
+        assert np.array_equal(q[last, tok_pad], b[:hd])
