@@ -150,17 +150,27 @@ int win_geom(const char* what, int64_t images, int h, int w, int ws, int nh, int
 template <typename T>
 int launch_split_window(const void* y, const void* bias, void* out, int64_t images, const WinGeom& g, cudaStream_t st) {
   const int64_t units = images * g.nwh * g.nww * g.nh;
-  const int gy = (g.n() + kWinTok - 1) / kWinTok;
+  const int chunk = win_chunk(g.n(), g.hd);
+  const int gy = (g.n() + chunk - 1) / chunk;
   if (units > 0x7fffffffLL || gy > 65535) return fail(SAMRS_ERR_UNSUPPORTED, "qkv_split_window: grid too large");
-  const size_t smem = (size_t)kWinTok * (g.hd + 1) * sizeof(float);
+  const size_t smem = (size_t)chunk * (g.hd + 1) * sizeof(float);
   constexpr int kVec = 16 / (int)sizeof(T);
+  constexpr int kKt = sizeof(T) == 2 ? 4 : 2;  // kt tokens per 8-byte store
   const dim3 grid((unsigned)units, gy);
-  if ((g.hd * (int)sizeof(T)) % 16 == 0 && aligned16_all(y, bias, out))
-    qkv_split_window_kernel<T, kVec><<<grid, 256, smem, st>>>(static_cast<const T*>(y), static_cast<const T*>(bias),
-                                                               static_cast<T*>(out), (long)units, g);
+  const auto* yp = static_cast<const T*>(y);
+  const auto* bp = static_cast<const T*>(bias);
+  auto* op = static_cast<T*>(out);
+  auto kvec = qkv_split_window_kernel<T, kVec, kKt>;
+  auto kone = qkv_split_window_kernel<T, 1, 1>;
+  const bool vec = (g.hd * (int)sizeof(T)) % 16 == 0 && aligned16_all(y, bias, out) && g.n() % kKt == 0 &&
+                   chunk % kKt == 0;
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(vec ? kvec : kone, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem) != cudaSuccess)
+    return fail(SAMRS_ERR_UNSUPPORTED, "qkv_split_window: cannot set %zu bytes of shared memory", smem);
+  if (vec)
+    kvec<<<grid, 256, smem, st>>>(yp, bp, op, (long)units, g);
   else
-    qkv_split_window_kernel<T, 1><<<grid, 256, smem, st>>>(static_cast<const T*>(y), static_cast<const T*>(bias),
-                                                            static_cast<T*>(out), (long)units, g);
+    kone<<<grid, 256, smem, st>>>(yp, bp, op, (long)units, g);
   return launch_status("qkv_split_window");
 }
 
@@ -170,12 +180,20 @@ int launch_merge(const void* attn, void* out, int64_t images, const WinGeom& g, 
   const bool vec = (g.hd * (int)sizeof(T)) % 16 == 0 && aligned16_all(attn, out, out);
   const int64_t chunks = images * g.h * (int64_t)g.w * g.c() / (vec ? kVec : 1);
   const int64_t blocks = std::min<int64_t>((chunks + 255) / 256, (int64_t)num_sms * 16);
-  if (vec)
-    window_merge_kernel<T, kVec><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const T*>(attn), static_cast<T*>(out),
-                                                                   (long)images, g);
+  // 32-bit indices when every source and destination element index fits
+  const int64_t elems = std::max<int64_t>(images * g.h * (int64_t)g.w * g.c(),
+                                          images * g.nwh * (int64_t)g.nww * g.nh * g.n() * g.hd);
+  const bool narrow = elems < (int64_t)0x7fffffff;
+  const auto* ap = static_cast<const T*>(attn);
+  auto* op = static_cast<T*>(out);
+  if (vec && narrow)
+    window_merge_kernel<T, kVec, uint32_t><<<(unsigned)blocks, 256, 0, st>>>(ap, op, (long)images, g);
+  else if (vec)
+    window_merge_kernel<T, kVec, uint64_t><<<(unsigned)blocks, 256, 0, st>>>(ap, op, (long)images, g);
+  else if (narrow)
+    window_merge_kernel<T, 1, uint32_t><<<(unsigned)blocks, 256, 0, st>>>(ap, op, (long)images, g);
   else
-    window_merge_kernel<T, 1><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const T*>(attn), static_cast<T*>(out),
-                                                                (long)images, g);
+    window_merge_kernel<T, 1, uint64_t><<<(unsigned)blocks, 256, 0, st>>>(ap, op, (long)images, g);
   return launch_status("window_merge");
 }
 

@@ -37,7 +37,15 @@ __device__ __forceinline__ long win_token_row(const WinGeom& g, long image, int 
   return (image * g.h + gy) * (long)g.w + gx;
 }
 
-constexpr int kWinTok = 32;  // tokens per CTA of the split
+// Tokens per CTA of the split: a whole window when it has at most 256 tokens (and its K block fits in
+// 96 KB of shared memory), else chunks of 64 tokens (fewer when hd is large; a multiple of 4).
+__host__ __device__ inline int win_chunk(int n, int hd) {
+  int cap = (96 * 1024) / ((hd + 1) * 4);
+  cap = cap < 256 ? cap : 256;
+  if (n <= cap) return n;
+  cap = (cap < 64 ? cap : 64) & ~3;
+  return cap < 4 ? 4 : cap;
+}
 
 // VEC elements of T moved as one access (16 bytes when VEC * sizeof(T) == 16).
 template <int BYTES>
@@ -68,14 +76,14 @@ union Pack {
   T e[VEC];
 };
 
-// blockIdx.x = unit = ((image * nwh + win_r) * nww + win_c) * nh + head; blockIdx.y = 32-token chunk.
-// q and v rows go out as VEC-element vectors; K goes through shared memory and out transposed, so both
-// the reads of y and the writes of kt are coalesced.
-template <typename T, int VEC>
+// blockIdx.x = unit = ((image * nwh + win_r) * nww + win_c) * nh + head; blockIdx.y = token chunk.
+// q and v rows go out as VEC-element vectors; K goes through shared memory and out transposed, KT tokens
+// per store, so both the reads of y and the writes of kt are coalesced.
+template <typename T, int VEC, int KT>
 __global__ void __launch_bounds__(256) qkv_split_window_kernel(const T* __restrict__ y, const T* __restrict__ bias,
                                                                T* __restrict__ outp, long units, WinGeom g) {
   extern __shared__ float4 smem_f4[];
-  float* kbuf = reinterpret_cast<float*>(smem_f4);  // [kWinTok][hd + 1]
+  float* kbuf = reinterpret_cast<float*>(smem_f4);  // [chunk][hd + 1]
   const long unit = blockIdx.x;
   const int n = g.n(), hd = g.hd;
   const long c = g.c();
@@ -83,9 +91,10 @@ __global__ void __launch_bounds__(256) qkv_split_window_kernel(const T* __restri
   const long win = unit / g.nh;
   const int win_c = (int)(win % g.nww), win_r = (int)((win / g.nww) % g.nwh);
   const long image = win / ((long)g.nww * g.nwh);
-  const int tok0 = blockIdx.y * kWinTok;
+  const int chunk = win_chunk(n, hd);
+  const int tok0 = blockIdx.y * chunk;
   if (tok0 >= n) return;
-  const int ntok = min(kWinTok, n - tok0);
+  const int ntok = min(chunk, n - tok0);
   const long plane = units * (long)n * hd;  // elements of each of q, kt, v
   T* qo = outp;
   T* ko = outp + plane;
@@ -122,32 +131,39 @@ __global__ void __launch_bounds__(256) qkv_split_window_kernel(const T* __restri
     *reinterpret_cast<V*>(vo + o) = ov.v;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < ntok * hd; idx += blockDim.x) {
-    const int d = idx / ntok, t = idx % ntok;
-    ko[(unit * hd + d) * (long)n + tok0 + t] = from_f<T>(kbuf[t * hdp + d]);
+  // kt rows: KT consecutive tokens of one dim per store (n and the chunk are multiples of KT)
+  const int ng = ntok / KT;
+  for (int idx = threadIdx.x; idx < ng * hd; idx += blockDim.x) {
+    const int d = idx / ng, t = (idx % ng) * KT;
+    Pack<T, KT> pk;
+#pragma unroll
+    for (int e = 0; e < KT; ++e) pk.e[e] = from_f<T>(kbuf[(t + e) * hdp + d]);
+    *reinterpret_cast<typename VecOf<T, KT>::type*>(ko + (unit * hd + d) * (long)n + tok0 + t) = pk.v;
   }
 }
 
 // One thread per VEC-element chunk of an output row (a chunk never straddles two heads: hd % VEC == 0).
-template <typename T, int VEC>
+// I is the index type: 32-bit when the chunk count allows (cheaper divisions), else 64-bit.
+template <typename T, int VEC, typename I>
 __global__ void __launch_bounds__(256) window_merge_kernel(const T* __restrict__ attn, T* __restrict__ out,
                                                            long images, WinGeom g) {
   using V = typename VecOf<T, VEC>::type;
-  const int c = g.c(), n = g.n();
-  const int cv = c / VEC;
-  const long total = images * g.h * (long)g.w * cv;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const long tokrow = i / cv;
-    const int ch = (int)(i % cv) * VEC;
-    const int head = ch / g.hd, d = ch % g.hd;
-    const int gx = (int)(tokrow % g.w);
-    const long rest = tokrow / g.w;
-    const int gy = (int)(rest % g.h);
-    const long image = rest / g.h;
-    const long win = (image * g.nwh + gy / g.wh) * g.nww + gx / g.ww;
-    const int tok = (gy % g.wh) * g.ww + gx % g.ww;
-    const long src = ((win * g.nh + head) * n + tok) * (long)g.hd + d;
-    *reinterpret_cast<V*>(out + tokrow * c + ch) = *reinterpret_cast<const V*>(attn + src);
+  const I c = (I)g.c(), n = (I)g.n(), hd = (I)g.hd, w = (I)g.w, h = (I)g.h;
+  const I cv = c / VEC;
+  const I total = (I)images * h * w * cv;
+  for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
+    const I tokrow = i / cv;
+    const I ch = (i - tokrow * cv) * VEC;
+    const I head = ch / hd, d = ch - head * hd;
+    const I rest = tokrow / w;
+    const I gx = tokrow - rest * w;
+    const I image = rest / h;
+    const I gy = rest - image * h;
+    const I wy = gy / (I)g.wh, wx = gx / (I)g.ww;
+    const I win = (image * (I)g.nwh + wy) * (I)g.nww + wx;
+    const I tok = (gy - wy * (I)g.wh) * (I)g.ww + (gx - wx * (I)g.ww);
+    const I src = ((win * (I)g.nh + head) * n + tok) * hd + d;
+    *reinterpret_cast<V*>(out + (size_t)tokrow * c + ch) = *reinterpret_cast<const V*>(attn + src);
   }
 }
 
