@@ -29,7 +29,8 @@
 // row = TMEM lane); warp 11 covers rows 224..255 only, which are all padding, so it only keeps the
 // barrier counts.
 // TMEM (512 columns): tile t owns [256t, 256t+256): S_t; then P_t (16-bit pairs, cols 0..103) written
-// over the consumed scores; O_t accumulates in cols [128, 128+hd) once the softmax has consumed S_t.
+// over the consumed scores; O_t and its row sums accumulate in cols [128, 128+hd+16) once the softmax
+// has consumed S_t (the P.V MMA multiplies by [V | ones]).
 #pragma once
 #include <cuda.h>
 
@@ -61,14 +62,18 @@ struct Layout {
   static constexpr int kQChunk = kQRows * 32;
   static constexpr int kQBytes = HC * kQChunk;
   static constexpr int kVChunk = kNP * 32;          // [208 keys x 32 B] SW32
-  static constexpr int kVBytes = HC * kVChunk;
+  static constexpr int kVBytes = HC * kVChunk;      // bytes of v loaded per unit
+  // The V stage holds the HC chunks of v and then a chunk of ones: the P.V MMA runs with N = HD + 16, so
+  // that O's last 16 columns accumulate the row sums of the 16-bit P exactly as the product uses them.
+  static constexpr int kVStageBytes = (HC + 1) * kVChunk;
+  static constexpr int kOCols = HD + 16;
   // B operand of the S MMA, N = 256: keys, then table rows. Stride between 8-column core columns: HD/8
   // core matrices of 128 B plus 16 B, so consecutive columns fall in different banks for the 8-byte
   // cp.async writes (2 wavefronts per warp, the minimum for 256 B).
   static constexpr int kKSbo = (HD / 8) * 128 + 16;
   static constexpr int kKBytes = (kNB / 8) * kKSbo;
   static constexpr int kQKStage = (kQBytes + kKBytes + 255) / 256 * 256;
-  static constexpr int kVStage = (kVBytes + 255) / 256 * 256;
+  static constexpr int kVStage = (kVStageBytes + 255) / 256 * 256;
   static constexpr int OFF_Q = 0, OFF_K = kQBytes;  // within a QK stage
   static constexpr int OFF_V = kStages * kQKStage;  // one V stage: loaded during the unit's softmax
   // output staging: the 128 rows of each tile (row-major, as in `out`), written back by bulk stores
@@ -134,12 +139,11 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&sv)[32], float2 c2, c
   }
 }
 
-// Pass 2 over chunk CH (keys 32*CH + e, e < NE): p = 2^(S*c + rh + (rw - m)); 4 pairwise partial sums;
-// 16-bit pairs into pk (keys >= 196 get p = 0).
+// Pass 2 over chunk CH (keys 32*CH + e, e < NE): p = 2^(S*c + rh + (rw - m)) as 16-bit pairs into pk
+// (keys >= 196 get p = 0). The row sums come from the P.V MMA (ones block of V).
 template <int CH, int NE, bool BF16>
-__device__ __forceinline__ void chunk_exp(const uint32_t (&sv)[32], float2 c2, const Bias& b, float2 (&sum)[4],
-                                          uint32_t (&pk)[16]) {
-  // Staged: all exponents, then the exponentials (one pair in four on the FMA pipe), then sums and packing.
+__device__ __forceinline__ void chunk_exp(const uint32_t (&sv)[32], float2 c2, const Bias& b, uint32_t (&pk)[16]) {
+  // Staged: all exponents, then the exponentials (one pair in four on the FMA pipe), then packing.
   constexpr int NV = (32 * CH + NE <= kN) ? NE : (kN - 32 * CH);  // keys of the chunk below kN (even)
   float x[32];
 #pragma unroll
@@ -162,14 +166,7 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&sv)[32], float2 c2, c
     }
   }
 #pragma unroll
-  for (int e = 0; e < NE; e += 2) {
-    float2 p = make_float2(0.f, 0.f);
-    if (e < NV) {
-      p = make_float2(x[e], x[e + 1]);
-      sum[(e >> 1) & 3] = sm100::add2(sum[(e >> 1) & 3], p);
-    }
-    pk[e >> 1] = sm100::pack2(p.x, p.y, BF16);
-  }
+  for (int e = 0; e < NE; e += 2) pk[e >> 1] = e < NV ? sm100::pack2(x[e], x[e + 1], BF16) : 0u;
 }
 
 // Row max over the 196 keys: two chunks per wait, the next two loads in flight while a pair is reduced.
@@ -203,50 +200,86 @@ __device__ __forceinline__ float row_max(uint32_t tS, float2 c2, const Bias& b) 
   return max3(max3(m[0], m[1], m[2]), max3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 
-// p = 2^(x - m) for all keys (the bias pairs already hold rw - m), row sum returned, P written as 16-bit
-// pairs over the consumed S columns 0..103. The load of chunk k+1 is in flight while chunk k is
-// exponentiated.
+// Max of the raw scores S over the 196 keys of chunk CH (8 independent maxima).
+template <int CH>
+__device__ __forceinline__ void chunk_smax(const uint32_t (&sv)[32], float (&m)[8]) {
+#pragma unroll
+  for (int e = 0; e < 32; e += 2)
+    if (32 * CH + e < kN) m[(e >> 1) & 7] = sm100::max3(m[(e >> 1) & 7], __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+}
+
+// Upper bound of the row max for bf16: c * max S + max rh + max rw (log2 units). It exceeds the true max
+// by at most the row's rh and rw spreads; any reference at or above the max gives the same softmax once the
+// row sums come from the rounded P (the ones block), and bf16 P holds 2^-126 .. 2^127. One max per key pair
+// instead of the exact pass's fma, add and max.
+__device__ __forceinline__ float row_max_bound(uint32_t tS, float c, float rhm, float rwm) {
+  using namespace sm100;
+  uint32_t a[32], bb[32], a2[32], bb2[32];
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = -INFINITY;
+  tmem_ld32(tS + 0, a);
+  tmem_ld32(tS + 32, bb);
+  tmem_wait_ld_regs(a);
+  tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 64, a2);
+  tmem_ld32(tS + 96, bb2);
+  chunk_smax<0>(a, m);
+  chunk_smax<1>(bb, m);
+  tmem_wait_ld_regs(a2);
+  tmem_wait_ld_regs(bb2);
+  tmem_ld32(tS + 128, a);
+  tmem_ld32(tS + 160, bb);
+  chunk_smax<2>(a2, m);
+  chunk_smax<3>(bb2, m);
+  tmem_wait_ld_regs(a);
+  tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 192, a2);  // columns 192..223: keys 192..195
+  chunk_smax<4>(a, m);
+  chunk_smax<5>(bb, m);
+  tmem_wait_ld_regs(a2);
+  chunk_smax<6>(a2, m);
+  const float ms = max3(max3(m[0], m[1], m[2]), max3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+  return ms * c + rhm + rwm;
+}
+
+// p = 2^(x - m) for all keys (the bias pairs already hold rw - m), P written as 16-bit pairs over the
+// consumed S columns 0..103. The load of chunk k+1 is in flight while chunk k is exponentiated.
 template <bool BF16>
-__device__ __forceinline__ float row_exp(uint32_t tS, float2 c2, const Bias& b) {
+__device__ __forceinline__ void row_exp(uint32_t tS, float2 c2, const Bias& b) {
   using namespace sm100;
   uint32_t a[32], bb[32], pk[16];
-  float2 sum[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) sum[i] = make_float2(0.f, 0.f);
   tmem_ld32(tS + 0, a);
   tmem_wait_ld_regs(a);
   tmem_ld32(tS + 32, bb);
-  chunk_exp<0, 32, BF16>(a, c2, b, sum, pk);
+  chunk_exp<0, 32, BF16>(a, c2, b, pk);
   tmem_st16(tS + 0, pk);
   tmem_wait_ld_regs(bb);
   tmem_ld32(tS + 64, a);
-  chunk_exp<1, 32, BF16>(bb, c2, b, sum, pk);
+  chunk_exp<1, 32, BF16>(bb, c2, b, pk);
   tmem_st16(tS + 16, pk);
   tmem_wait_ld_regs(a);
   tmem_ld32(tS + 96, bb);
-  chunk_exp<2, 32, BF16>(a, c2, b, sum, pk);
+  chunk_exp<2, 32, BF16>(a, c2, b, pk);
   tmem_st16(tS + 32, pk);
   tmem_wait_ld_regs(bb);
   tmem_ld32(tS + 128, a);
-  chunk_exp<3, 32, BF16>(bb, c2, b, sum, pk);
+  chunk_exp<3, 32, BF16>(bb, c2, b, pk);
   tmem_st16(tS + 48, pk);
   tmem_wait_ld_regs(a);
   tmem_ld32(tS + 160, bb);
-  chunk_exp<4, 32, BF16>(a, c2, b, sum, pk);
+  chunk_exp<4, 32, BF16>(a, c2, b, pk);
   tmem_st16(tS + 64, pk);
   tmem_wait_ld_regs(bb);
   tmem_ld32(tS + 192, a);
-  chunk_exp<5, 32, BF16>(bb, c2, b, sum, pk);
+  chunk_exp<5, 32, BF16>(bb, c2, b, pk);
   tmem_st16(tS + 80, pk);
   tmem_wait_ld_regs(a);
-  chunk_exp<6, 16, BF16>(a, c2, b, sum, pk);  // keys 192..207 (196.. get p = 0)
+  chunk_exp<6, 16, BF16>(a, c2, b, pk);  // keys 192..207 (196.. get p = 0)
   uint32_t p8[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) p8[e] = pk[e];
   tmem_st8(tS + 96, p8);
-  const float2 s01 = add2(sum[0], sum[1]), s23 = add2(sum[2], sum[3]);
-  const float2 st = add2(s01, s23);
-  return st.x + st.y;
 }
 
 // Bias of this thread's row from the S columns 192..255: rh from RH (cols 196..222) shifted by the grid
@@ -312,6 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
   }
+  {
+    // the ones block of the V stage (the TMA loads never write it); read by the MMA (async proxy)
+    const uint32_t one2 = kBf16 ? 0x3F803F80u : 0x3C003C00u;
+    for (int idx = threadIdx.x; idx < L::kVChunk / 16; idx += kThreads)
+      reinterpret_cast<uint4*>(smem + L::OFF_V + L::HC * L::kVChunk)[idx] = make_uint4(one2, one2, one2, one2);
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -324,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The whole warp runs the issue loop; lane 0, elected inside each MMA and commit, issues them.
       const int t = 1 - warp;
       constexpr uint32_t idS = idesc_f16(kBf16, 128, kNB, false, true);
-      constexpr uint32_t idPV = idesc_f16(kBf16, 128, HD, false, true);
+      constexpr uint32_t idPV = idesc_f16(kBf16, 128, L::kOCols, false, true);  // O += P [V | 1]
       const uint32_t sb = smem_u32(smem);
       const uint64_t dQ = smem_desc(sb + L::OFF_Q + t * 128 * 32, 16, 256, kLayoutSw32);
       const uint64_t dK = smem_desc(sb + L::OFF_K, 128, L::kKSbo, kLayoutNone);
@@ -438,15 +478,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long u = first + (long)ui * gridDim.x;
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[t], ui & 1, abort_flag))) break;
       tc_fence_after();
-      float sum = 1.f;
       if (live) {
         Bias b;
         read_bias(tS, i, j, b);
         const float2 c2 = make_float2(c, c);
-        const float m = row_max(tS, c2, b);
+        float m;
+        bool exact = !kBf16 || !(c > 0.f);
+        float rhm = -INFINITY, rwm = -INFINITY, rhn = INFINITY, rwn = INFINITY;
+        if (!exact) {
+#pragma unroll
+          for (int k = 0; k < 14; ++k) {
+            rhm = fmaxf(rhm, b.rhp[k].x);
+            rhn = fminf(rhn, b.rhp[k].x);
+          }
+#pragma unroll
+          for (int k = 0; k < 7; ++k) {
+            rwm = max3(rwm, b.rwp[k].x, b.rwp[k].y);
+            rwn = fminf(rwn, fminf(b.rwp[k].x, b.rwp[k].y));
+          }
+          // the bound is at most the rh and rw spreads above the max; keep P of the largest scores
+          // (>= 2^-96) far from the bottom of bf16's range (the whole warp takes the exact pass otherwise)
+          exact = __any_sync(0xffffffffu, (rhm - rhn) + (rwm - rwn) > 96.f);
+        }
+        if (exact)
+          m = row_max(tS, c2, b);
+        else
+          m = row_max_bound(tS, c, rhm, rwm);
 #pragma unroll
         for (int k = 0; k < 7; ++k) b.rwp[k] = make_float2(b.rwp[k].x - m, b.rwp[k].y - m);
-        sum = row_exp<kBf16>(tS, c2, b);
+        row_exp<kBf16>(tS, c2, b);
         tmem_wait_st();
       }
       tc_fence_before();
@@ -454,16 +514,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&bars->p_full[t]);
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_full[t], ui & 1, abort_flag))) break;
       tc_fence_after();
-      // Epilogue: O/l into registers, the tile's TMEM columns handed back at once (the next unit's S MMA
-      // may overwrite them), then the row's 16-byte stores.
+      // Epilogue: O/l into registers (l = any column of the ones block), the tile's TMEM columns handed
+      // back at once (the next unit's S MMA may overwrite them), then the row's 16-byte stores.
       uint32_t pw[HD / 16][8];
       if (live) {
-        const float inv = 1.f / sum;
-        uint32_t ov[HD / 16][16];
+        uint32_t ov[HD / 16 + 1][16];
 #pragma unroll
-        for (int c0 = 0; c0 < HD / 16; ++c0) tmem_ld16(tO + 16 * c0, ov[c0]);
+        for (int c0 = 0; c0 <= HD / 16; ++c0) tmem_ld16(tO + 16 * c0, ov[c0]);
 #pragma unroll
-        for (int c0 = 0; c0 < HD / 16; ++c0) tmem_wait_ld_regs(ov[c0]);
+        for (int c0 = 0; c0 <= HD / 16; ++c0) tmem_wait_ld_regs(ov[c0]);
+        const float inv = 1.f / __uint_as_float(ov[HD / 16][0]);
 #pragma unroll
         for (int c0 = 0; c0 < HD / 16; ++c0)
 #pragma unroll

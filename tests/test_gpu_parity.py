@@ -149,6 +149,29 @@ def test_global_late_max_jumps(samrs, cuda, hd, dt):
     assert err < HALF_TOL, err
 
 
+@pytest.mark.parametrize("table_std", [0.1, 0.5, 8.0])
+@pytest.mark.parametrize("hd", [64, 80])
+def test_window_bf16_row_max_bound(samrs, cuda, hd, table_std):
+    """bf16 windowed layers take the row max as c * max S + max rh + max rw (above the true max by the
+    row's bias spreads) unless a row's spreads exceed 96 log2 units, when the warp takes the exact max:
+    small tables (bound), the bench's N(0, 0.5) (bound), N(0, 8) (exact). A few keys with large scores
+    make rows dominated by one key."""
+    h = w = 14
+    q, kt, v, t = make_inputs(h, w, 40, hd, seed=hd + int(table_std * 10), table_std=table_std)
+    kt[::3, :, 17] *= 6.0
+    err = parity_err(*_run_window_bf16(samrs, cuda, q, kt, v, t, hd), "bf16")
+    assert err < HALF_TOL, err
+
+
+def _run_window_bf16(samrs, cuda, q, kt, v, t, hd):
+    scale = hd ** -0.5
+    qd, ktd, vd, td = (to_dev(x, "bf16", cuda) for x in (q, kt, v, t))
+    out = samrs.attention_relpos(qd, ktd, vd, td, 14, 14, scale)
+    assert samrs.device_status() == 0
+    ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), 14, 14, scale)
+    return out.float().cpu().numpy(), ref
+
+
 @pytest.mark.parametrize("hd", [64, 80])
 def test_global_bf16_overflow_recompute(samrs, cuda, hd):
     """bf16 global layers: a CTA whose single-pass tiles would overflow is recomputed exactly.
