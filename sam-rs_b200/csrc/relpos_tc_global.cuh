@@ -57,10 +57,10 @@ constexpr int kBQ = 128, kBK = 128, kSide = 64, kN = 4096, kNT = kN / kBK, kStag
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 // bf16: speculative single-pass tiles (see the softmax). The predicted max is capped kSpecCap above the
-// row's running max, the reference is raised once the prediction passes it by kSpecRaise, and a CTA whose
-// tiles saw an exponent above kSpecLimit (P > 2^64) or a non-finite output is recomputed exactly by a
-// second launch.
-constexpr float kSpecCap = 64.f, kSpecRaise = 4.f, kSpecLimit = 64.f;
+// row's running max (P of the dominant keys >= 2^-100, well inside bf16's normal range), the reference is
+// raised once the prediction passes it by kSpecRaise, and a CTA whose tiles saw an exponent above
+// kSpecLimit (P > 2^112) or a non-finite output is recomputed exactly by a second launch.
+constexpr float kSpecCap = 96.f, kSpecRaise = 4.f, kSpecLimit = 112.f;
 // Kernel modes: the exact two-pass softmax (f16); the speculative pass (bf16), which marks a CTA that needs
 // the exact pass by a NaN in the first element of its output block; the exact pass of the marked CTAs
 // only (bf16, launched right after the speculative one; the others return at once).
