@@ -56,11 +56,11 @@ static_assert(128 * kRegsLow + 512 * kRegsHigh <= kThreads * kLaunchRegs, "regis
 constexpr int kBQ = 128, kBK = 128, kSide = 64, kN = 4096, kNT = kN / kBK, kStages = 2;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
-// bf16: speculative single-pass tiles (see the softmax). The predicted max is capped kSpecCap above the
-// row's running max (P of the dominant keys >= 2^-100, well inside bf16's normal range), the reference is
-// raised once the prediction passes it by kSpecRaise, and a CTA whose tiles saw an exponent above
-// kSpecLimit (P > 2^112) or a non-finite output is recomputed exactly by a second launch.
-constexpr float kSpecCap = 96.f, kSpecRaise = 4.f, kSpecLimit = 112.f;
+// bf16: single-pass tiles against one reference per row fixed at tile 0 (see the softmax). The reference
+// is capped kSpecCap above the row's max over tile 0 (P of the dominant keys >= 2^-96, well inside bf16's
+// normal range), and a CTA whose tiles saw an exponent above kSpecLimit (P > 2^112) or a non-finite output
+// is recomputed exactly by a second launch.
+constexpr float kSpecCap = 96.f, kSpecLimit = 112.f;
 // Kernel modes: the exact two-pass softmax (f16); the speculative pass (bf16), which marks a CTA that needs
 // the exact pass by a NaN in the first element of its output block; the exact pass of the marked CTAs
 // only (bf16, launched right after the speculative one; the others return at once).
@@ -533,9 +533,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       });
     };
     // Exact tile: pass 1 gives the row maxima t of S*c + rw + rh (rh per 64-key half) across the row's four
-    // threads (and, if base is given, the maxima of S*c + rw), then pass 2 against the raised reference.
+    // threads, then pass 2 against the raised reference.
     auto exact_tile = [&](int j, float rhA0, float rhA1, float rhB0, float rhB1, float& alA, float& alB,
-                          bool& needA, bool& needB, float& tA, float& tB, float* bA_out, float* bB_out) {
+                          bool& needA, bool& needB, float& tA, float& tB) {
       {
         uint32_t v0[8], v1[8];
         float mA[2] = {-INFINITY, -INFINITY}, mB[2] = {-INFINITY, -INFINITY};
@@ -554,15 +554,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 1));
         tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 2));
         tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 2));
-        if (bA_out) {
-          float bA = fmaxf(mA[0], mA[1]), bB = fmaxf(mB[0], mB[1]);
-          bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 1));
-          bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 1));
-          bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 2));
-          bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 2));
-          *bA_out = bA;
-          *bB_out = bB;
-        }
       }
       needA = (j == 0) || (tA > mrA + kRescaleThreshold);
       needB = (j == 0) || (tB > mrB + kRescaleThreshold);
@@ -649,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
         bool needA, needB;
         float alA = 1.f, alB = 1.f, tA, tB;
-        exact_tile(j, rhA0, rhA1, rhB0, rhB1, alA, alB, needA, needB, tA, tB, nullptr, nullptr);
+        exact_tile(j, rhA0, rhA1, rhB0, rhB1, alA, alB, needA, needB, tA, tB);
         finish_tile(j, needA, needB, alA, alB);
       }
       epilogue(pass);
@@ -657,14 +648,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (MODE != kModeSpec) {
       exact_pass(0);
     } else {
-      // Speculative pass (bf16): the first tile exact, the others in a single pass. Per row: run = the
-      // running max of the full score, base = that of S*c + rw (without the per-key-row rh term), rhmax =
-      // the largest rh over all key rows. base + rhmax bounds a tile's max unless the base grows within it;
-      // the prediction is that bound capped kSpecCap above run, and the reference is raised to it once it
-      // passes the reference by kSpecRaise. Any reference gives the same softmax (O and its row sums scale
-      // together) and bf16 P and the f32 sums hold 2^-126 .. 2^127: the exponents are tracked, and if one
-      // exceeds kSpecLimit or an output is not finite, the CTA leaves the NaN marker for the fixup launch.
-      float runA, runB, baseA, baseB, rhmaxA = -INFINITY, rhmaxB = -INFINITY;
+      // Speculative pass (bf16): one pass per tile against one reference per row, set at tile 0 from its
+      // row max pass: base = max over tile 0 of S*c + rw (the score without the per-key-row rh term;
+      // tile 0 covers every key column, so every rw), rhmax = the largest rh over all 64 key rows, and the
+      // reference = min(base + rhmax, t + kSpecCap) with t tile 0's max of the full score. base + rhmax
+      // bounds every later score unless S*c + rw grows beyond tile 0's, so later exponents stay near or
+      // below 0; the cap keeps the dominant keys' P above 2^-96. Any reference gives the same softmax (O
+      // and its row sums from the ones block scale together) and bf16 P and the f32 sums hold 2^-126 ..
+      // 2^127: the exponents are tracked, and if one exceeds kSpecLimit or an output is not finite, the CTA
+      // leaves the NaN marker for the fixup launch. No O rescale is ever needed.
+      float rhmaxA = -INFINITY, rhmaxB = -INFINITY;
       bool unsafe = false;
       for (int j = 0; j < kNT && okk; ++j) {
         okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
@@ -672,46 +665,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float rhA0 = rh_park[(2 * j) * 256 + prowA], rhA1 = rh_park[(2 * j + 1) * 256 + prowA];
         const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
-        bool needA, needB;
-        float alA = 1.f, alB = 1.f;
+        const bool needA = false, needB = false;
+        const float alA = 1.f, alB = 1.f;
+        float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (j == 0) {
 #pragma unroll 8
           for (int kh = 0; kh < 64; ++kh) {
             rhmaxA = fmaxf(rhmaxA, rh_park[kh * 256 + prowA]);
             rhmaxB = fmaxf(rhmaxB, rh_park[kh * 256 + prowB]);
           }
-          exact_tile(j, rhA0, rhA1, rhB0, rhB1, alA, alB, needA, needB, runA, runB, &baseA, &baseB);
-        } else {
-          const float pA = fminf(baseA + rhmaxA, runA + kSpecCap), pB = fminf(baseB + rhmaxB, runB + kSpecCap);
-          needA = pA > mrA + kSpecRaise;
-          needB = pB > mrB + kSpecRaise;
-          if (needA) {
-            alA = ex2(mrA - pA);
-            mrA = pA;
-          }
-          if (needB) {
-            alB = ex2(mrB - pB);
-            mrB = pB;
-          }
-          float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-          pass2(std::integral_constant<bool, true>{}, rhA0, rhA1, rhB0, rhB1, xm);
-          unsafe |= fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])) > kSpecLimit;
-          // the tile's base and max: the exponent maxima + m (- rh), across the row's four threads
-          float bA = fmaxf(xm[0] - rhA0, xm[1] - rhA1) + mrA, bB = fmaxf(xm[2] - rhB0, xm[3] - rhB1) + mrB;
-          float uA = fmaxf(xm[0], xm[1]) + mrA, uB = fmaxf(xm[2], xm[3]) + mrB;
+          uint32_t v0[8], v1[8];
+          float mA[2] = {-INFINITY, -INFINITY}, mB[2] = {-INFINITY, -INFINITY};
+          static_for<0, 4>([&](auto kk) {
+            constexpr int k = decltype(kk)::value;
+            tmem_ld_16x256b_x2(tS + 32 * k, v0);
+            tmem_ld_16x256b_x2(tS + 32 * k + 16, v1);
+            tmem_wait_ld_regs(v0);
+            tmem_wait_ld_regs(v1);
+            chunk_max<4 * k>(v0, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
+            chunk_max<4 * k + 2>(v1, c2, rwA, rwB, mA[k >> 1], mB[k >> 1]);
+          });
+          float tA = fmaxf(mA[0] + rhA0, mA[1] + rhA1), tB = fmaxf(mB[0] + rhB0, mB[1] + rhB1);
+          float bA = fmaxf(mA[0], mA[1]), bB = fmaxf(mB[0], mB[1]);
+          tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 1));
+          tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 1));
           bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 1));
           bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 1));
-          uA = fmaxf(uA, __shfl_xor_sync(0xffffffffu, uA, 1));
-          uB = fmaxf(uB, __shfl_xor_sync(0xffffffffu, uB, 1));
+          tA = fmaxf(tA, __shfl_xor_sync(0xffffffffu, tA, 2));
+          tB = fmaxf(tB, __shfl_xor_sync(0xffffffffu, tB, 2));
           bA = fmaxf(bA, __shfl_xor_sync(0xffffffffu, bA, 2));
           bB = fmaxf(bB, __shfl_xor_sync(0xffffffffu, bB, 2));
-          uA = fmaxf(uA, __shfl_xor_sync(0xffffffffu, uA, 2));
-          uB = fmaxf(uB, __shfl_xor_sync(0xffffffffu, uB, 2));
-          baseA = fmaxf(baseA, bA);
-          baseB = fmaxf(baseB, bB);
-          runA = fmaxf(runA, uA);
-          runB = fmaxf(runB, uB);
+          mrA = fminf(bA + rhmaxA, tA + kSpecCap);
+          mrB = fminf(bB + rhmaxB, tB + kSpecCap);
         }
+        pass2(std::integral_constant<bool, true>{}, rhA0, rhA1, rhB0, rhB1, xm);
+        unsafe |= fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])) > kSpecLimit;
         finish_tile(j, needA, needB, alA, alB);
       }
       unsafe |= !epilogue(0);
