@@ -97,7 +97,8 @@ struct Bars {
   uint64_t q_full, pro_done, final_mma;
   uint64_t k_full[kStages], v_full[kStages], k_empty[kStages], v_empty[kStages];
   uint64_t bias_done[2], s_full[2], p_full[2], o_done[2];
-  uint64_t epi_done;  // speculative pass: every softmax warp has written its outputs and flag
+  uint64_t epi_done;
+  uint64_t p_half[2];  // speculative pass: P of the first 64 keys written (one arrival per softmax warp)  // speculative pass: every softmax warp has written its outputs and flag
   uint32_t tmem_base;
   int abort_flag;
   int rerun;  // speculative pass: a softmax thread asks for the exact pass
@@ -291,6 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->s_full[q], 1);
       mbar_init(&bars->p_full[q], 8);
       mbar_init(&bars->o_done[q], 1);
+      mbar_init(&bars->p_half[q], 8);
     }
     mbar_init(&bars->epi_done, 16);  // one arrival per softmax warp
     bars->abort_flag = 0;
@@ -423,13 +425,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             // still runs), then the softmax's P: PV_q(j) and S_q(j+1) issue back to back
             if (q == 0) okk = wait(&bars->v_full[st], (j / kStages) & 1);
             if (okk && q == 0 && j + 1 < kNT) okk = wait(&bars->k_full[st1], ((j + 1) / kStages) & 1);
+            int s0 = 0;
+            if constexpr (MODE == kModeSpec) {
+              // the first half of P.V as soon as the softmax has written P of keys 0..63
+              if (okk) okk = wait(&bars->p_half[q], j & 1);
+              if (!okk) break;
+              tc_fence_after();
+#pragma unroll
+              for (int s = 0; s < kBK / 32; ++s)
+                mma_ts_w(tmem + 256 + q * L::kOCols, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV,
+                         s > 0 ? 1u : acc0);
+              s0 = kBK / 32;
+            }
             if (okk) okk = wait(&bars->p_full[q], j & 1);
             if (!okk) break;
             tc_fence_after();
 #pragma unroll
             for (int s = 0; s < kBK / 16; ++s)
-              mma_ts_w(tmem + 256 + q * L::kOCols, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV,
-                       s > 0 ? 1u : acc0);
+              if (s >= s0)
+                mma_ts_w(tmem + 256 + q * L::kOCols, tmem + q * 128 + s * 8, desc_add(dVs, s * 512), idPV,
+                         s > 0 ? 1u : acc0);
             if (j + 1 < kNT) {
               // issued after PV_q(j), which reads P_q(j) from the same columns: in-order execution
               issue_s(q, st1);
@@ -512,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // pairs, columns 8k..8k+7) lands on scores of chunk k/2 <= k, already read. The load of chunk k+1 is in
     // flight meanwhile. TRACK: the largest exponent per (row, 64-key half) into xm (A0, A1, B0, B1).
     float mrA = -INFINITY, mrB = -INFINITY;
-    auto pass2 = [&](auto track, float rhA0, float rhA1, float rhB0, float rhB1, float (&xm)[4]) {
+    auto pass2 = [&](auto track, float rhA0, float rhA1, float rhB0, float rhB1, float (&xm)[4], bool half) {
       constexpr bool kTrack = decltype(track)::value;
       const float2 bA0 = make_float2(rhA0 - mrA, rhA0 - mrA), bA1 = make_float2(rhA1 - mrA, rhA1 - mrA);
       const float2 bB0 = make_float2(rhB0 - mrB, rhB0 - mrB), bB1 = make_float2(rhB1 - mrB, rhB1 - mrB);
@@ -529,6 +544,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         else
           chunk_exp<2 * k, kBf16, kTrack>(cur, c2, rwA, rwB, bA1, bB1, pw, xm[1], xm[3]);
         tmem_st_16x128b_x2(tS + 8 * k, pw);
+        if constexpr (k == 3) {
+          if (half) {  // P of keys 0..63 is complete: the first half of P.V may start
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->p_half[q]);
+          }
+        }
         if constexpr (k + 1 < 8) tmem_wait_ld_regs(nxt);
       });
     };
@@ -568,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mrB = mn;
       }
       float xm[4];
-      pass2(std::integral_constant<bool, false>{}, rhA0, rhA1, rhB0, rhB1, xm);
+      pass2(std::integral_constant<bool, false>{}, rhA0, rhA1, rhB0, rhB1, xm, false);
     };
     // End of a tile: O and row-sum rescale (PV_q(j-1) has completed: it was issued before S_q(j), whose
     // commit we waited on), then one P-ready arrival per warp once every lane's P and O stores are done.
@@ -698,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mrA = fminf(bA + rhmaxA, tA + kSpecCap);
           mrB = fminf(bB + rhmaxB, tB + kSpecCap);
         }
-        pass2(std::integral_constant<bool, true>{}, rhA0, rhA1, rhB0, rhB1, xm);
+        pass2(std::integral_constant<bool, true>{}, rhA0, rhA1, rhB0, rhB1, xm, true);
         unsafe |= fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])) > kSpecLimit;
         finish_tile(j, needA, needB, alA, alB);
       }
