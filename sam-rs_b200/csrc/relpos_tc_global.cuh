@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (q == 0) okk = wait(&bars->v_full[st], (j / kStages) & 1);
             if (okk && q == 0 && j + 1 < kNT) okk = wait(&bars->k_full[st1], ((j + 1) / kStages) & 1);
             int s0 = 0;
-            if constexpr (MODE == kModeSpec) {
+            {
               // the first half of P.V as soon as the softmax has written P of keys 0..63
               if (okk) okk = wait(&bars->p_half[q], j & 1);
               if (!okk) break;
@@ -555,6 +555,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (k + 1 < 8) tmem_wait_ld_regs(nxt);
       });
     };
+    // O and row-sum rescale by (alA, alB) where the reference was raised: PV_q(j-1) has completed (it was
+    // issued before S_q(j), whose commit was waited on), and PV_q(j) starts only once P of the tile's first
+    // 64 keys is written, after this.
+    auto rescale_o = [&](int j, bool needA, bool needB, float alA, float alB) {
+      if (__any_sync(0xffffffffu, (needA || needB) && j > 0)) {
+#pragma unroll
+        for (int c0 = 0; c0 < L::kOCols; c0 += 16) {
+          uint32_t ov[8];
+          tmem_ld_16x256b_x2(tO + c0, ov);
+          tmem_wait_ld_regs(ov);
+          ov[0] = __float_as_uint(__uint_as_float(ov[0]) * alA);
+          ov[1] = __float_as_uint(__uint_as_float(ov[1]) * alA);
+          ov[4] = __float_as_uint(__uint_as_float(ov[4]) * alA);
+          ov[5] = __float_as_uint(__uint_as_float(ov[5]) * alA);
+          ov[2] = __float_as_uint(__uint_as_float(ov[2]) * alB);
+          ov[3] = __float_as_uint(__uint_as_float(ov[3]) * alB);
+          ov[6] = __float_as_uint(__uint_as_float(ov[6]) * alB);
+          ov[7] = __float_as_uint(__uint_as_float(ov[7]) * alB);
+          tmem_st_16x256b_x2(tO + c0, ov);
+        }
+      }
+    };
     // Exact tile: pass 1 gives the row maxima t of S*c + rw + rh (rh per 64-key half) across the row's four
     // threads, then pass 2 against the raised reference.
     auto exact_tile = [&](int j, float rhA0, float rhA1, float rhB0, float rhB1, float& alA, float& alB,
@@ -590,29 +612,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         alB = ex2(mrB - mn);
         mrB = mn;
       }
+      rescale_o(j, needA, needB, alA, alB);
       float xm[4];
-      pass2(std::integral_constant<bool, false>{}, rhA0, rhA1, rhB0, rhB1, xm, false);
+      pass2(std::integral_constant<bool, false>{}, rhA0, rhA1, rhB0, rhB1, xm, true);
     };
-    // End of a tile: O and row-sum rescale (PV_q(j-1) has completed: it was issued before S_q(j), whose
-    // commit we waited on), then one P-ready arrival per warp once every lane's P and O stores are done.
-    auto finish_tile = [&](int j, bool needA, bool needB, float alA, float alB) {
-      if (__any_sync(0xffffffffu, (needA || needB) && j > 0)) {
-#pragma unroll
-        for (int c0 = 0; c0 < L::kOCols; c0 += 16) {
-          uint32_t ov[8];
-          tmem_ld_16x256b_x2(tO + c0, ov);
-          tmem_wait_ld_regs(ov);
-          ov[0] = __float_as_uint(__uint_as_float(ov[0]) * alA);
-          ov[1] = __float_as_uint(__uint_as_float(ov[1]) * alA);
-          ov[4] = __float_as_uint(__uint_as_float(ov[4]) * alA);
-          ov[5] = __float_as_uint(__uint_as_float(ov[5]) * alA);
-          ov[2] = __float_as_uint(__uint_as_float(ov[2]) * alB);
-          ov[3] = __float_as_uint(__uint_as_float(ov[3]) * alB);
-          ov[6] = __float_as_uint(__uint_as_float(ov[6]) * alB);
-          ov[7] = __float_as_uint(__uint_as_float(ov[7]) * alB);
-          tmem_st_16x256b_x2(tO + c0, ov);
-        }
-      }
+    // End of a tile: one P-ready arrival per warp once every lane's P stores are done.
+    auto finish_tile = [&]() {
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -664,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool needA, needB;
         float alA = 1.f, alB = 1.f, tA, tB;
         exact_tile(j, rhA0, rhA1, rhB0, rhB1, alA, alB, needA, needB, tA, tB);
-        finish_tile(j, needA, needB, alA, alB);
+        finish_tile();
       }
       epilogue(pass);
     };
@@ -688,8 +693,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float rhA0 = rh_park[(2 * j) * 256 + prowA], rhA1 = rh_park[(2 * j + 1) * 256 + prowA];
         const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
-        const bool needA = false, needB = false;
-        const float alA = 1.f, alB = 1.f;
         float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (j == 0) {
 #pragma unroll 8
@@ -723,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         pass2(std::integral_constant<bool, true>{}, rhA0, rhA1, rhB0, rhB1, xm, true);
         unsafe |= fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])) > kSpecLimit;
-        finish_tile(j, needA, needB, alA, alB);
+        finish_tile();
       }
       unsafe |= !epilogue(0);
       // The marker goes in after its element's own output (written by this very thread of warp 4 in its
