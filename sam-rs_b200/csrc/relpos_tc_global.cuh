@@ -234,14 +234,10 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, con
     xmA = sm100::max3(xmA, sm100::max3(x[0], x[1], x[4]), x[5]);
     xmB = sm100::max3(xmB, sm100::max3(x[2], x[3], x[6]), x[7]);
   }
-  // 6 of the 8 exponentials on the exp unit, the row-B pair of the second block on the FMA pipe
+  // all on the exp unit (with the single pass it has room: moving a pair in four to the FMA pipe's
+  // polynomial measured slower)
 #pragma unroll
-  for (int i = 0; i < 6; ++i) x[i] = sm100::ex2(x[i]);
-  {
-    const float2 pe = sm100::ex2_poly2(make_float2(x[6], x[7]));
-    x[6] = pe.x;
-    x[7] = pe.y;
-  }
+  for (int i = 0; i < 8; ++i) x[i] = sm100::ex2(x[i]);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     pw[2 * i] = sm100::pack2(x[4 * i], x[4 * i + 1], BF16);
