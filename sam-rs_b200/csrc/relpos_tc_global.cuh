@@ -58,9 +58,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 // bf16: single-pass tiles against one reference per row fixed at tile 0 (see the softmax). The reference
 // is capped kSpecCap above the row's max over tile 0 (P of the dominant keys >= 2^-96, well inside bf16's
-// normal range), and a CTA whose tiles saw an exponent above kSpecLimit (P > 2^112) or a non-finite output
-// is recomputed exactly by a second launch.
+// normal range), and a CTA with a row whose largest P exceeded 2^kSpecLimit (seen as a row sum of 2^112 or
+// more) or with a non-finite output is recomputed exactly by a second launch.
 constexpr float kSpecCap = 96.f, kSpecLimit = 112.f;
+constexpr float kSpecSumLimit = 0x1p112f;  // 2^kSpecLimit
 // Kernel modes: the exact two-pass softmax (f16); the speculative pass (bf16), which marks a CTA that needs
 // the exact pass by a NaN in the first element of its output block; the exact pass of the marked CTAs
 // only (bf16, launched right after the speculative one; the others return at once).
@@ -212,11 +213,9 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&v)[8], float2 c2, con
 // Pass 2: p = 2^(S*c + rw + (rh - m)) for both rows as 16-bit pairs in the 16x128b store order (pw[2i]
 // row A, pw[2i+1] row B: P column 4(G0+i) + c = keys 8(G0+i) + 2c, +1). Staged (exponents, then the ex2,
 // then packing) so the ex2 issue back to back. The row sums come from the P.V MMA (ones block of V).
-// TRACK: also the largest exponent per row (xmA, xmB).
-template <int G0, bool BF16, bool TRACK>
+template <int G0, bool BF16>
 __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, const float2 (&rwA)[8],
-                                          const float2 (&rwB)[8], float2 bA, float2 bB, uint32_t (&pw)[4],
-                                          float& xmA, float& xmB) {
+                                          const float2 (&rwB)[8], float2 bA, float2 bB, uint32_t (&pw)[4]) {
   float x[8];
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
@@ -229,10 +228,6 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&v)[8], float2 c2, con
     x[4 * i + 1] = xa.y;
     x[4 * i + 2] = xb.x;
     x[4 * i + 3] = xb.y;
-  }
-  if constexpr (TRACK) {  // x[0,1,4,5] row A, x[2,3,6,7] row B
-    xmA = sm100::max3(xmA, sm100::max3(x[0], x[1], x[4]), x[5]);
-    xmB = sm100::max3(xmB, sm100::max3(x[2], x[3], x[6]), x[7]);
   }
   // all on the exp unit (with the single pass it has room: moving a pair in four to the FMA pipe's
   // polynomial measured slower)
@@ -521,10 +516,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // pass 2 over the tile with reference maxima (mrA, mrB): p = 2^(S*c + rw + rh - m); P of chunk k (16-bit
     // pairs, columns 8k..8k+7) lands on scores of chunk k/2 <= k, already read. The load of chunk k+1 is in
-    // flight meanwhile. TRACK: the largest exponent per (row, 64-key half) into xm (A0, A1, B0, B1).
+    // flight meanwhile. Once P of keys 0..63 is written the warp arrives on p_half (the first half of P.V
+    // may start).
     float mrA = -INFINITY, mrB = -INFINITY;
-    auto pass2 = [&](auto track, float rhA0, float rhA1, float rhB0, float rhB1, float (&xm)[4], bool half) {
-      constexpr bool kTrack = decltype(track)::value;
+    auto pass2 = [&](float rhA0, float rhA1, float rhB0, float rhB1) {
       const float2 bA0 = make_float2(rhA0 - mrA, rhA0 - mrA), bA1 = make_float2(rhA1 - mrA, rhA1 - mrA);
       const float2 bB0 = make_float2(rhB0 - mrB, rhB0 - mrB), bB1 = make_float2(rhB1 - mrB, rhB1 - mrB);
       uint32_t v0[8], v1[8], pw[4];
@@ -536,17 +531,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t(&nxt)[8] = (k & 1) ? v0 : v1;
         if constexpr (k + 1 < 8) tmem_ld_16x256b_x2(tS + 16 * (k + 1), nxt);
         if constexpr (k < 4)
-          chunk_exp<2 * k, kBf16, kTrack>(cur, c2, rwA, rwB, bA0, bB0, pw, xm[0], xm[2]);
+          chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA0, bB0, pw);
         else
-          chunk_exp<2 * k, kBf16, kTrack>(cur, c2, rwA, rwB, bA1, bB1, pw, xm[1], xm[3]);
+          chunk_exp<2 * k, kBf16>(cur, c2, rwA, rwB, bA1, bB1, pw);
         tmem_st_16x128b_x2(tS + 8 * k, pw);
         if constexpr (k == 3) {
-          if (half) {  // P of keys 0..63 is complete: the first half of P.V may start
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_half[q]);
-          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->p_half[q]);
         }
         if constexpr (k + 1 < 8) tmem_wait_ld_regs(nxt);
       });
@@ -609,8 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mrB = mn;
       }
       rescale_o(j, needA, needB, alA, alB);
-      float xm[4];
-      pass2(std::integral_constant<bool, false>{}, rhA0, rhA1, rhB0, rhB1, xm, true);
+      pass2(rhA0, rhA1, rhB0, rhB1);
     };
     // End of a tile: one P-ready arrival per warp once every lane's P stores are done.
     auto finish_tile = [&]() {
@@ -631,6 +623,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_16x256b_x2(tO + HD, lv);
         tmem_wait_ld_regs(lv);
         const float invA = 1.f / __uint_as_float(lv[0]), invB = 1.f / __uint_as_float(lv[2]);
+        // the row sum is at least the row's largest P: a sum of 2^kSpecLimit or more (or a NaN) means an
+        // exponent above kSpecLimit somewhere in the row
+        finite &= __uint_as_float(lv[0]) < kSpecSumLimit && __uint_as_float(lv[2]) < kSpecSumLimit;
         T* oA = out + (bh * kN + row0 + prowA) * HD + 2 * c;
         T* oB = oA + 8 * HD;
 #pragma unroll
@@ -679,17 +674,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       // bounds every later score unless S*c + rw grows beyond tile 0's, so later exponents stay near or
       // below 0; the cap keeps the dominant keys' P above 2^-96. Any reference gives the same softmax (O
       // and its row sums from the ones block scale together) and bf16 P and the f32 sums hold 2^-126 ..
-      // 2^127: the exponents are tracked, and if one exceeds kSpecLimit or an output is not finite, the CTA
-      // leaves the NaN marker for the fixup launch. No O rescale is ever needed.
+      // 2^127: the epilogue checks each row sum (at least the row's largest P) against 2^kSpecLimit and
+      // each output for finiteness, and a CTA that fails either leaves the NaN marker for the fixup launch.
+      // No O rescale is ever needed.
       float rhmaxA = -INFINITY, rhmaxB = -INFINITY;
-      bool unsafe = false;
       for (int j = 0; j < kNT && okk; ++j) {
         okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
         if (!okk) break;
         tc_fence_after();
         const float rhA0 = rh_park[(2 * j) * 256 + prowA], rhA1 = rh_park[(2 * j + 1) * 256 + prowA];
         const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
-        float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (j == 0) {
 #pragma unroll 8
           for (int kh = 0; kh < 64; ++kh) {
@@ -720,11 +714,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           mrA = fminf(bA + rhmaxA, tA + kSpecCap);
           mrB = fminf(bB + rhmaxB, tB + kSpecCap);
         }
-        pass2(std::integral_constant<bool, true>{}, rhA0, rhA1, rhB0, rhB1, xm, true);
-        unsafe |= fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])) > kSpecLimit;
+        pass2(rhA0, rhA1, rhB0, rhB1);
         finish_tile();
       }
-      unsafe |= !epilogue(0);
+      const bool unsafe = !epilogue(0);
       // The marker goes in after its element's own output (written by this very thread of warp 4 in its
       // epilogue) and after every warp's flag.
       if (__any_sync(0xffffffffu, unsafe) && lane == 0) bars->rerun = 1;
