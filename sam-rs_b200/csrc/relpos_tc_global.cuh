@@ -21,10 +21,10 @@
 //                the exp unit busy while the other query tile waits on its MMAs.
 //
 // Rel-pos bias, computed in-tile: the prologue MMAs give RW = Q Tw^T (128 cols) and RH = Q Th[I0..I0+79]^T
-// (80 cols) in TMEM. rw: each warp reads RW for its lane quarter, a lane-dependent barrel shift selects
-// row r's window j..j+63 (reversed, = rw[kw]) and shuffles hand each thread the 16 values of its key
-// pairs for its two rows (log2 units, in registers). rh: parked in shared memory as [kh][row]; a key tile
-// needs two rh values per row (one per 64-key half).
+// (80 cols) in TMEM. Each query row owns 64 words of shared memory (the park), used twice: first the two
+// warps of a lane quarter write each row's window RW[r][j .. j+63] there reversed (= rw[kw], log2 units)
+// and every thread reads the 16 values of its key pairs for its two rows into registers; then the row's
+// 64 rh values are parked there for the key tiles (two per tile and row, one per 64-key half).
 // The softmax is online in the log2 domain; P is written back as 16-bit pairs into the S columns of TMEM
 // and fed to the P.V MMA as the A operand straight from TMEM. The V stages carry a block of ones, so the
 // MMA also accumulates the row sums of P as rounded. Exact mode (f16): two passes per tile, O rescaled only
@@ -79,7 +79,7 @@ struct Layout {
   // that O's last 16 columns accumulate the row sums of the 16-bit P exactly as the product uses them.
   static constexpr int kVStage = (HC + 1) * kChunkBytes;
   static constexpr int kOCols = HD + 16;
-  static constexpr int kRhBytes = 64 * 256 * 4;       // rh park: [kh][256 rows] f32
+  static constexpr int kRhBytes = 256 * 64 * 4;       // park: [256 rows][64] f32 (rw staging, then rh)
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * kQBytes;
   static constexpr int OFF_V = OFF_K + kStages * kKBytes;
@@ -88,7 +88,8 @@ struct Layout {
   static constexpr int OFF_TW = OFF_RH + kQBytes;
   static constexpr int OFF_BAR = OFF_RH + kRhBytes;
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = OFF_BAR + kBarBytes + 1024;  // + alignment slack
+  static constexpr int OFF_RHMAX = OFF_BAR + kBarBytes;  // [2][256 rows] f32: the largest rh of each row
+  static constexpr int kSmemBytes = OFF_RHMAX + 2 * 256 * 4 + 1024;  // + alignment slack
   static_assert(2 * kQBytes <= kRhBytes, "tables must fit in the rh park");
   static_assert(kKAtom % 1024 == 0 && OFF_K % 1024 == 0 && OFF_V % 1024 == 0, "SW128 atoms need 1 KB alignment");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -99,96 +100,76 @@ struct Bars {
   uint64_t k_full[kStages], v_full[kStages], k_empty[kStages], v_empty[kStages];
   uint64_t bias_done[2], s_full[2], p_full[2], o_done[2];
   uint64_t epi_done;
-  uint64_t p_half[2];  // speculative pass: P of the first 64 keys written (one arrival per softmax warp)  // speculative pass: every softmax warp has written its outputs and flag
+  uint64_t p_half[2];  // P of the first 64 keys written (one arrival per softmax warp)
+  uint64_t stg[8];     // per lane quarter (4q + wq), one arrival per warp: rw staged (phase 0), read (1)
   uint32_t tmem_base;
   int abort_flag;
   int rerun;  // speculative pass: a softmax thread asks for the exact pass
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
 
-// One stage of the lane-dependent shift: a[m] <- a[m + 2^B] where bit B of the lane is set.
-template <int B, int LEN>
-__device__ __forceinline__ void shift_stage(uint32_t (&a)[48], int lane) {
-  const uint32_t mask = 0u - ((uint32_t)(lane >> B) & 1u);
-#pragma unroll
-  for (int m = 0; m < LEN; ++m) a[m] = (a[m] & ~mask) | (a[m + (1 << B)] & mask);
-}
-
-// rw block C of the row on this lane (32x32b access): blk[i] = rw[16C + i] (log2 units). tW addresses the
-// lane quarter at column jb = 32*(warp&1); the lane's window starts at jb + lane + 48 - 16C.
-template <int C>
-__device__ __forceinline__ void rw_block(uint32_t tW, int lane, float (&blk)[16]) {
+// rw staging, one lane per query row (32x32b): row r = 32wq + lane of the quarter has grid column
+// j = jb + lane (jb = 32(wq & 1)), and rw[kw] = RW[r][j + 63 - kw]. The warp of 16-lane half hh loads the
+// window columns jb + 48hh .. jb + 48hh + 47 and writes each value whose kw lies in 0..63 to
+// row[kw ^ sw] (sw = 8 (r & 3): the 16x256b readers of eight consecutive rows then hit distinct banks).
+__device__ __forceinline__ void stage_rw(uint32_t tW, int lane, int hh, float* row, int sw) {
   using namespace sm100;
-  uint32_t a[48];
+  const int c0 = 48 * hh;
+  uint32_t v[32];
+  tmem_ld32(tW + c0, v);
+  tmem_wait_ld_regs(v);
 #pragma unroll
-  for (int b = 0; b < 3; ++b) {
-    uint32_t v[16];
-    tmem_ld16(tW + 48 - 16 * C + 16 * b, v);
-    tmem_wait_ld_regs(v);
-#pragma unroll
-    for (int e = 0; e < 16; ++e) a[16 * b + e] = v[e];
+  for (int i = 0; i < 32; ++i) {
+    const int kw = lane + 63 - (c0 + i);
+    if (kw >= 0 && kw < 64) row[kw ^ sw] = __uint_as_float(v[i]) * kLog2e;
   }
-  shift_stage<4, 31>(a, lane);
-  shift_stage<3, 23>(a, lane);
-  shift_stage<2, 19>(a, lane);
-  shift_stage<1, 17>(a, lane);
-  shift_stage<0, 16>(a, lane);
-  // a[e] = RW[r][j + 48 - 16C + e] = rw[kw] with kw = 15 + 16C - e
+  uint32_t u[16];
+  tmem_ld16(tW + c0 + 32, u);
+  tmem_wait_ld_regs(u);
 #pragma unroll
-  for (int e = 0; e < 16; ++e) blk[15 - e] = __uint_as_float(a[e]) * kLog2e;
+  for (int i = 0; i < 16; ++i) {
+    const int kw = lane + 63 - (c0 + 32 + i);
+    if (kw >= 0 && kw < 64) row[kw ^ sw] = __uint_as_float(u[i]) * kLog2e;
+  }
 }
 
-// Hands block C (rw[16C .. 16C+15] of every lane's row) to the 16x256b owners: the thread keeps
-// rwA[m] = (rw[8m + 2c], rw[8m + 2c + 1]) of row srcA and rwB[m] of row srcA + 8, for m = 2C, 2C+1.
-template <int C>
-__device__ __forceinline__ void rw_scatter(const float (&blk)[16], int srcA, int c, float2 (&rwA)[8],
-                                           float2 (&rwB)[8]) {
+// rh park of one row (32x32b, lane = row): row[kh ^ rl] = RH[OFF + 63 - kh] (log2 units) for the kh
+// whose column OFF + 63 - kh lies in COL0 .. COL0 + N - 1 (held in v); mx tracks their maximum. rl = the
+// row's low five bits, so the per-tile reads of eight consecutive rows hit distinct banks.
+template <int OFF, int COL0, int N>
+__device__ __forceinline__ void park_rh(const uint32_t* v, float* row, int rl, float& mx) {
 #pragma unroll
-  for (int mm = 0; mm < 2; ++mm) {
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float va = 0.f, vb = 0.f;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const float sa = __shfl_sync(0xffffffffu, blk[8 * mm + 2 * cc + e], srcA);
-        const float sb = __shfl_sync(0xffffffffu, blk[8 * mm + 2 * cc + e], srcA + 8);
-        va = cc == c ? sa : va;
-        vb = cc == c ? sb : vb;
-      }
-      if (e == 0) {
-        rwA[2 * C + mm].x = va;
-        rwB[2 * C + mm].x = vb;
-      } else {
-        rwA[2 * C + mm].y = va;
-        rwB[2 * C + mm].y = vb;
-      }
+  for (int cc = 0; cc < N; ++cc) {
+    const int kh = OFF + 63 - (COL0 + cc);
+    if (kh >= 0 && kh < 64) {
+      const float x = __uint_as_float(v[cc]) * kLog2e;
+      row[kh ^ rl] = x;
+      mx = fmaxf(mx, x);
     }
   }
 }
-
-// rh_park[kh][prow] = RH[OFF + 63 - kh] (log2 units) for the kh whose column OFF + 63 - kh lies in block B
-// (columns 32B .. 32B+31, held in v).
-template <int OFF, int B>
-__device__ __forceinline__ void park_rh(const uint32_t (&v)[32], float* rh_park, int prow) {
-#pragma unroll
-  for (int cc = 0; cc < 32; ++cc) {
-    const int kh = OFF + 63 - (32 * B + cc);
-    if (kh >= 0 && kh < 64) rh_park[kh * 256 + prow] = __uint_as_float(v[cc]) * kLog2e;
-  }
-}
+// The 64 rh of the row, split between the two warps of the quarter (hh 0: columns 0..31, hh 1: 32..79,
+// of which only OFF + 63 and below hold a kh); the warp's partial maximum goes to rhmax[hh][prow].
 template <int OFF>
-__device__ __forceinline__ void park_rh_all(uint32_t tRH, float* rh_park, int prow) {
+__device__ __forceinline__ void park_rh_half(uint32_t tRH, int hh, float* row, int rl, float* rhmax, int prow) {
   using namespace sm100;
-  uint32_t v[32];
-  tmem_ld32(tRH, v);
-  tmem_wait_ld_regs(v);
-  park_rh<OFF, 0>(v, rh_park, prow);
-  tmem_ld32(tRH + 32, v);
-  tmem_wait_ld_regs(v);
-  park_rh<OFF, 1>(v, rh_park, prow);
-  tmem_ld32(tRH + 64, v);
-  tmem_wait_ld_regs(v);
-  park_rh<OFF, 2>(v, rh_park, prow);
+  float mx = -INFINITY;
+  if (hh == 0) {
+    uint32_t v[32];
+    tmem_ld32(tRH, v);
+    tmem_wait_ld_regs(v);
+    park_rh<OFF, 0, 32>(v, row, rl, mx);
+  } else {
+    uint32_t v[32];
+    tmem_ld32(tRH + 32, v);
+    tmem_wait_ld_regs(v);
+    park_rh<OFF, 32, 32>(v, row, rl, mx);
+    uint32_t u[16];
+    tmem_ld16(tRH + 64, u);
+    tmem_wait_ld_regs(u);
+    park_rh<OFF, 64, 16>(u, row, rl, mx);
+  }
+  rhmax[hh * 256 + prow] = mx;
 }
 
 // Key block g = 0..15 of a tile holds keys 8g..8g+7 (64-key half g/8, rw index g%8); this thread's keys
@@ -253,6 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + L::OFF_BAR);
   float* rh_park = reinterpret_cast<float*>(smem + L::OFF_RH);
+  float* rhmax_park = reinterpret_cast<float*>(smem + L::OFF_RHMAX);
   volatile int* abort_flag = &bars->abort_flag;
 
   if (device_faulted()) return;  // an earlier CTA reported a fault: do no more work
@@ -286,9 +268,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->p_half[q], 8);
     }
     mbar_init(&bars->epi_done, 16);  // one arrival per softmax warp
+    for (int i = 0; i < 8; ++i) mbar_init(&bars->stg[i], 2);
     bars->abort_flag = 0;
     bars->rerun = 0;
     fence_mbar_init();
+    // Q0, Q1 and the two table slices, issued before the TMEM allocation and the CTA barrier (thread 0 is
+    // the producer's lane 0)
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    mbar_arrive_expect_tx(&bars->q_full, 4 * L::kQBytes);
+    for (int q = 0; q < 2; ++q)
+      for (int c = 0; c < L::HC; ++c)
+        tma_load_2d(smem + L::OFF_Q + q * L::kQBytes + c * L::kChunkBytes, &tmQ, &bars->q_full, c * 16,
+                    (int)(bh * kN + row0 + q * kBQ));
+    for (int c = 0; c < L::HC; ++c) {
+      tma_load_2d(smem + L::OFF_TH + c * L::kChunkBytes, &tmT, &bars->q_full, c * 16, I0);             // Th[I0..]
+      tma_load_2d(smem + L::OFF_TW + c * L::kChunkBytes, &tmT, &bars->q_full, c * 16, 2 * kSide - 1);  // Tw
+    }
   }
   if (warp == 2) {
     tmem_alloc(&bars->tmem_base, 512);
@@ -312,22 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     regs_dec<kRegsLow>();
     if (warp == 0) {
       // ---------------------------------------------------------------- TMA producer
-      if (lane == 0) {
-        tma_prefetch_desc(&tmQ);
-        tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmV);
-        tma_prefetch_desc(&tmT);
-        mbar_arrive_expect_tx(&bars->q_full, 4 * L::kQBytes);
-        for (int q = 0; q < 2; ++q)
-          for (int c = 0; c < L::HC; ++c)
-            tma_load_2d(smem + L::OFF_Q + q * L::kQBytes + c * L::kChunkBytes, &tmQ, &bars->q_full, c * 16,
-                        (int)(bh * kN + row0 + q * kBQ));
-        for (int c = 0; c < L::HC; ++c) {
-          tma_load_2d(smem + L::OFF_TH + c * L::kChunkBytes, &tmT, &bars->q_full, c * 16, I0);             // Th[I0..]
-          tma_load_2d(smem + L::OFF_TW + c * L::kChunkBytes, &tmT, &bars->q_full, c * 16, 2 * kSide - 1);  // Tw
-        }
-      }
-      // K and V of every key tile
+      // (Q and the tables went out with the barrier set-up) K and V of every key tile
       int issued_k = 0, issued_v = 0;
       if (lane == 0) {
         for (int j = 0; j < kNT; ++j) {
@@ -473,42 +454,48 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (okk) {
       tc_fence_after();
       const uint32_t tQuarter = tmem + ((uint32_t)(32 * wq) << 16);
-      // rh (one warp per lane quarter, 32x32b): RH_q[r][c'] = q_r . Th[I0 + c']. Row r of tile q sits on
-      // grid row i = I0 + 2q + r/64, so rh[kh] = q_r . Th[i - kh + 63] = RH_q[r][off + 63 - kh] with
-      // off = 2q + r/64 (warp-uniform). The park aliases the tables, which only the prologue MMAs read
-      // (they completed before pro_done).
-      if (hh == 0) {
-        const uint32_t tRH = tQuarter + 256 + q * 80;
-        const int prow = q * 128 + 32 * wq + lane;
-        switch (2 * q + (wq >> 1)) {
-          case 0:
-            park_rh_all<0>(tRH, rh_park, prow);
-            break;
-          case 1:
-            park_rh_all<1>(tRH, rh_park, prow);
-            break;
-          case 2:
-            park_rh_all<2>(tRH, rh_park, prow);
-            break;
-          default:
-            park_rh_all<3>(tRH, rh_park, prow);
-            break;
+      // The quarter's 32 rows (32x32b view: lane = row); the park aliases the tables, which only the
+      // prologue MMAs read (they completed before pro_done).
+      const int qi = 4 * q + wq;
+      const int srow = q * 128 + 32 * wq + lane;
+      float* const park_row = rh_park + srow * 64;
+      // rw: each row's window staged in its park row, then each thread reads its key pairs of rows A, B
+      stage_rw(tQuarter + q * 128 + 32 * (wq & 1), lane, hh, park_row, 8 * (srow & 3));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->stg[qi]);
+      okk = __all_sync(0xffffffffu, mbar_wait(&bars->stg[qi], 0, abort_flag));
+      {
+        const float* ra = rh_park + prowA * 64;
+        const float* rb = rh_park + prowB * 64;
+        const int sw = 8 * (prowA & 3);  // the same for prowB = prowA + 8
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          rwA[m] = *reinterpret_cast<const float2*>(ra + ((8 * m + 2 * c) ^ sw));
+          rwB[m] = *reinterpret_cast<const float2*>(rb + ((8 * m + 2 * c) ^ sw));
         }
       }
-      // rw: row r = 32wq + lane of the quarter has j = 32*(wq&1) + lane; its window RW[r][j .. j+63]
-      // reversed is rw[0..63]. Blocks of 16 are built per lane, then shuffled to the 16x256b owners.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->stg[qi]);
+      okk = okk && __all_sync(0xffffffffu, mbar_wait(&bars->stg[qi], 1, abort_flag));
+      // rh: RH_q[r][c'] = q_r . Th[I0 + c']. Row r of tile q sits on grid row i = I0 + 2q + r/64, so
+      // rh[kh] = q_r . Th[i - kh + 63] = RH_q[r][off + 63 - kh] with off = 2q + r/64 (warp-uniform).
       {
-        const uint32_t tW = tQuarter + q * 128 + 32 * (wq & 1);
-        const int srcA = 16 * hh + (lane >> 2);
-        float blk[16];
-        rw_block<0>(tW, lane, blk);
-        rw_scatter<0>(blk, srcA, c, rwA, rwB);
-        rw_block<1>(tW, lane, blk);
-        rw_scatter<1>(blk, srcA, c, rwA, rwB);
-        rw_block<2>(tW, lane, blk);
-        rw_scatter<2>(blk, srcA, c, rwA, rwB);
-        rw_block<3>(tW, lane, blk);
-        rw_scatter<3>(blk, srcA, c, rwA, rwB);
+        const uint32_t tRH = tQuarter + 256 + q * 80;
+        const int rl = srow & 31;
+        switch (2 * q + (wq >> 1)) {
+          case 0:
+            park_rh_half<0>(tRH, hh, park_row, rl, rhmax_park, srow);
+            break;
+          case 1:
+            park_rh_half<1>(tRH, hh, park_row, rl, rhmax_park, srow);
+            break;
+          case 2:
+            park_rh_half<2>(tRH, hh, park_row, rl, rhmax_park, srow);
+            break;
+          default:
+            park_rh_half<3>(tRH, hh, park_row, rl, rhmax_park, srow);
+            break;
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -519,6 +506,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // flight meanwhile. Once P of keys 0..63 is written the warp arrives on p_half (the first half of P.V
     // may start).
     float mrA = -INFINITY, mrB = -INFINITY;
+    // this thread's rows of the rh park (row-swizzled by the low five row bits)
+    const float* const rhA_row = rh_park + prowA * 64;
+    const float* const rhB_row = rh_park + prowB * 64;
+    const int rlA = prowA & 31, rlB = prowB & 31;
     auto pass2 = [&](float rhA0, float rhA1, float rhB0, float rhB1) {
       const float2 bA0 = make_float2(rhA0 - mrA, rhA0 - mrA), bA1 = make_float2(rhA1 - mrA, rhA1 - mrA);
       const float2 bB0 = make_float2(rhB0 - mrB, rhB0 - mrB), bB1 = make_float2(rhB1 - mrB, rhB1 - mrB);
@@ -655,8 +646,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
         if (!okk) break;
         tc_fence_after();
-        const float rhA0 = rh_park[(2 * j) * 256 + prowA], rhA1 = rh_park[(2 * j + 1) * 256 + prowA];
-        const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
+        const float rhA0 = rhA_row[(2 * j) ^ rlA], rhA1 = rhA_row[(2 * j + 1) ^ rlA];
+        const float rhB0 = rhB_row[(2 * j) ^ rlB], rhB1 = rhB_row[(2 * j + 1) ^ rlB];
         bool needA, needB;
         float alA = 1.f, alB = 1.f, tA, tB;
         exact_tile(j, rhA0, rhA1, rhB0, rhB1, alA, alB, needA, needB, tA, tB);
@@ -677,19 +668,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 2^127: the epilogue checks each row sum (at least the row's largest P) against 2^kSpecLimit and
       // each output for finiteness, and a CTA that fails either leaves the NaN marker for the fixup launch.
       // No O rescale is ever needed.
-      float rhmaxA = -INFINITY, rhmaxB = -INFINITY;
+      float rhmaxA, rhmaxB;
       for (int j = 0; j < kNT && okk; ++j) {
         okk = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, abort_flag));
         if (!okk) break;
         tc_fence_after();
-        const float rhA0 = rh_park[(2 * j) * 256 + prowA], rhA1 = rh_park[(2 * j + 1) * 256 + prowA];
-        const float rhB0 = rh_park[(2 * j) * 256 + prowB], rhB1 = rh_park[(2 * j + 1) * 256 + prowB];
+        const float rhA0 = rhA_row[(2 * j) ^ rlA], rhA1 = rhA_row[(2 * j + 1) ^ rlA];
+        const float rhB0 = rhB_row[(2 * j) ^ rlB], rhB1 = rhB_row[(2 * j + 1) ^ rlB];
         if (j == 0) {
-#pragma unroll 8
-          for (int kh = 0; kh < 64; ++kh) {
-            rhmaxA = fmaxf(rhmaxA, rh_park[kh * 256 + prowA]);
-            rhmaxB = fmaxf(rhmaxB, rh_park[kh * 256 + prowB]);
-          }
+          rhmaxA = fmaxf(rhmax_park[prowA], rhmax_park[256 + prowA]);
+          rhmaxB = fmaxf(rhmax_park[prowB], rhmax_park[256 + prowB]);
           uint32_t v0[8], v1[8];
           float mA[2] = {-INFINITY, -INFINITY}, mB[2] = {-INFINITY, -INFINITY};
           static_for<0, 4>([&](auto kk) {
