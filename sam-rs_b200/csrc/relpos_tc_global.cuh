@@ -115,17 +115,16 @@ static_assert(sizeof(Bars) <= 256, "barrier block");
 __device__ __forceinline__ void stage_rw(uint32_t tW, int lane, int hh, float* row, int sw) {
   using namespace sm100;
   const int c0 = 48 * hh;
-  uint32_t v[32];
+  uint32_t v[32], u[16];
   tmem_ld32(tW + c0, v);
+  tmem_ld16(tW + c0 + 32, u);
   tmem_wait_ld_regs(v);
+  tmem_wait_ld_regs(u);
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const int kw = lane + 63 - (c0 + i);
     if (kw >= 0 && kw < 64) row[kw ^ sw] = __uint_as_float(v[i]) * kLog2e;
   }
-  uint32_t u[16];
-  tmem_ld16(tW + c0 + 32, u);
-  tmem_wait_ld_regs(u);
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int kw = lane + 63 - (c0 + 32 + i);
@@ -375,18 +374,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                      desc_add(dTh, c * L::kChunkBytes), idRH, c > 0);
         }
         mma_commit_w(&bars->pro_done);
-        // S_q overwrites RW_q and the rh park aliases the tables: both query tiles must be done with them
-        okk = wait(&bars->bias_done[0], 0) && wait(&bars->bias_done[1], 0) && wait(&bars->k_full[0], 0);
+        okk = wait(&bars->k_full[0], 0);
       }
       {
-        if (okk) {
+        // S_q(0) overwrites RW_q: once query tile q's warps have read it (their bias_done)
+        for (int q = 0; q < 2 && okk; ++q) {
+          okk = wait(&bars->bias_done[q], 0);
+          if (!okk) break;
           tc_fence_after();
-          issue_s(0, 0);
-          mma_commit_w(&bars->s_full[0]);
-          issue_s(1, 0);
-          mma_commit_w(&bars->s_full[1]);
-          mma_commit_w(&bars->k_empty[0]);
+          issue_s(q, 0);
+          mma_commit_w(&bars->s_full[q]);
         }
+        if (okk) mma_commit_w(&bars->k_empty[0]);
         for (int j = 0; j < kNT && okk; ++j) {
           const int st = j % kStages, st1 = (j + 1) % kStages;
           const uint64_t dVs = desc_add(dV, st * L::kVStage);
