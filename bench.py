@@ -1,23 +1,28 @@
 #!/usr/bin/env python
-"""Benchmark of the fused decomposed-rel-pos attention on B200 ("config 4").
+"""Benchmark of the fused decomposed-rel-pos attention on B200 (4 and 5).
 
-One step = one pass of SAM ViT-H's encoder attention over a batch of synthetic inputs resident in HBM:
-32 layers in encoder order (src/sam1/encoder.rs:23 VIT_H: global attention at layers 7, 15, 23, 31, 14x14
-windowed attention elsewhere), 32 images per GPU, bf16, 16 heads, head_dim 80:
-    global layer   : bh = 32*16      = 512   heads of 64x64 = 4096 tokens
-    windowed layer : bh = 32*25*16   = 12800 windows-heads of 14x14 = 196 tokens (64x64 grid padded to 70x70)
-Algorithmic FLOPs: 4*N^2*hd per head (QK^T + PV); 481.3 GFLOP per image, 15.40 TFLOP per step per GPU.
+One step = one pass of a SAM ViT encoder's attention over a batch of synthetic inputs resident in HBM, all
+layers in encoder order (src/sam1/encoder.rs:19-23), bf16:
+    config 4 (default, the metric's configuration): ViT-H, 32 images per GPU, 16 heads, head_dim 80, 32 layers,
+        global attention at layers 7, 15, 23, 31 and 14x14 windowed attention elsewhere:
+        global layer   : bh = 32*16      = 512   heads of 64x64 = 4096 tokens
+        windowed layer : bh = 32*25*16   = 12800 windows-heads of 14x14 = 196 tokens (64x64 padded to 70x70)
+        481.3 GFLOP per image, 15.40 TFLOP per step per GPU (4*N^2*hd per head: QK^T + PV)
+    config 3: ViT-L, 16 images per GPU, 16 heads, head_dim 64, 24 layers, global at 5, 11, 17, 23
+    config 5: config 4 swept over 8, 16, 32, 64 and 128 images per GPU
+The default run prints the config-4 line and carries configs 3 and 5 (shorter timings of the same kind) in
+its "configs" object; --config 3 / 5 print their own line.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 3|4|5]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N   (one rank per GPU)
 
-Multi-GPU: the image batch is sharded (32 images per rank, weak scaling); there is no collective in the
-data path. NCCL is used after the timed region to take the max of the per-rank device times and to
+Multi-GPU: the image batch is sharded (the per-GPU image count is fixed, weak scaling); there is no collective
+in the data path. NCCL is used after the timed region to take the max of the per-rank device times and to
 gather per-rank output checksums.
 
 --impl reference times the reference's CPU implementation of the path (the C restatement under
 oracle/, the reference itself being Rust that cannot be built here) on the host cores of rank 0, on a
-bounded sample of the same workload (whole images, all 32 layers).
+bounded sample of the same workload (whole images, all layers).
 """
 import argparse
 import ctypes
@@ -35,19 +40,38 @@ if ROOT not in sys.path:
 
 METRIC = "fused rel-pos attn TFLOP/s (SAM ViT-H encoder attention, 32 layers) & images/s"
 UNIT = "TFLOP/s"
-HEADS, HD, DEPTH = 16, 80, 32
-GLOBAL_LAYERS = (7, 15, 23, 31)
 WINDOWS = 25  # 64x64 tokens padded to 70x70 -> 5x5 windows of 14x14
+KINDS = ("global", "window")  # fixed order: inputs are drawn from the generator in this order
 
 
-def layer_geoms(images):
-    """[(kind, h, w, bh)] for the 32 layers of one step."""
+class Workload:
+    """One ViT's attention stack (src/sam1/encoder.rs:19-23: VIT_L, VIT_H)."""
+
+    def __init__(self, name, heads, hd, depth, global_layers, images):
+        self.name, self.heads, self.hd, self.depth = name, heads, hd, depth
+        self.global_layers, self.images = tuple(global_layers), images
+
+    def describe(self):
+        return (f"{self.name} encoder attention (rel-pos), bf16, {self.depth} layers (global "
+                f"{','.join(map(str, self.global_layers))} / windowed 14x14), head_dim {self.hd}, {self.heads} heads")
+
+
+VIT_H = dict(name="SAM ViT-H", heads=16, hd=80, depth=32, global_layers=(7, 15, 23, 31))
+VIT_L = dict(name="SAM ViT-L", heads=16, hd=64, depth=24, global_layers=(5, 11, 17, 23))
+CONFIGS = {3: Workload(images=16, **VIT_L), 4: Workload(images=32, **VIT_H)}
+SWEEP_IMAGES = (8, 16, 32, 64, 128)  # config 5: config 4 at these images per GPU
+HD = VIT_H["hd"]
+
+
+def layer_geoms(images, wl=None):
+    """[(kind, h, w, bh)] for the layers of one step, in encoder order."""
+    wl = wl or CONFIGS[4]
     out = []
-    for layer in range(DEPTH):
-        if layer in GLOBAL_LAYERS:
-            out.append(("global", 64, 64, images * HEADS))
+    for layer in range(wl.depth):
+        if layer in wl.global_layers:
+            out.append(("global", 64, 64, images * wl.heads))
         else:
-            out.append(("window", 14, 14, images * WINDOWS * HEADS))
+            out.append(("window", 14, 14, images * WINDOWS * wl.heads))
     return out
 
 
@@ -170,31 +194,34 @@ class ClockSampler:
 # CPU reference arm / CPU baseline
 # --------------------------------------------------------------------------------------------
 
-def cpu_sample(images=1, seed=7):
+def cpu_sample(images=1, seed=7, wl=None):
     """Time the reference's CPU path (oracle restatement) on `images` whole images of the workload.
     Returns (tflops, seconds, sample description, threads, kind-of-path)."""
     import numpy as np
     from oracle import oracle
+    wl = wl or CONFIGS[4]
     mode = "bf16" if oracle.cpu_has_bf16() else "exact"
     # all host threads this process may use (torchrun sets OMP_NUM_THREADS=1 for its workers)
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     rng = np.random.default_rng(seed)
+    geoms = layer_geoms(images, wl)
     sets = {}
-    for kind, h, w, bh in {g[:3] + (g[3],) for g in layer_geoms(images)}:
+    for kind in KINDS:
+        _, h, w, bh = next(g for g in geoms if g[0] == kind)
         n = h * w
-        sets[kind] = (rng.standard_normal((bh, n, HD), dtype=np.float32),
-                      rng.standard_normal((bh, HD, n), dtype=np.float32),
-                      rng.standard_normal((bh, n, HD), dtype=np.float32),
-                      (rng.standard_normal((4 * h - 2, HD), dtype=np.float32) * 0.5).astype(np.float32), h, w)
+        sets[kind] = (rng.standard_normal((bh, n, wl.hd), dtype=np.float32),
+                      rng.standard_normal((bh, wl.hd, n), dtype=np.float32),
+                      rng.standard_normal((bh, n, wl.hd), dtype=np.float32),
+                      (rng.standard_normal((4 * h - 2, wl.hd), dtype=np.float32) * 0.5).astype(np.float32), h, w)
     flops = 0.0
     t0 = time.perf_counter()
-    for kind, h, w, bh in layer_geoms(images):
+    for kind, h, w, bh in geoms:
         q, kt, v, t, _, _ = sets[kind]
-        oracle.attention_relpos(q, kt, v, t, h, w, HD ** -0.5, threads=threads, mode=mode)
-        flops += layer_flops(h, w, bh)
+        oracle.attention_relpos(q, kt, v, t, h, w, wl.hd ** -0.5, threads=threads, mode=mode)
+        flops += layer_flops(h, w, bh, wl.hd)
     dt = time.perf_counter() - t0
-    desc = (f"{images} image(s) x 32 layers of the config-4 workload ({mode} CPU path of src/kernels.rs:131-225"
-            f"{' + src/cpu_gemm.rs' if mode == 'bf16' else ''}), {threads} threads")
+    desc = (f"{images} image(s) x {wl.depth} layers of the {wl.name} workload ({mode} CPU path of "
+            f"src/kernels.rs:131-225{' + src/cpu_gemm.rs' if mode == 'bf16' else ''}), {threads} threads")
     return flops / dt / 1e12, dt, desc, threads, mode
 
 
@@ -202,12 +229,13 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    wl = CONFIGS[3 if args.config == 3 else 4]
     for _ in range(args.warmup):
-        cpu_sample(images=1)
+        cpu_sample(images=1, wl=wl)
     vals, secs = [], []
     desc, threads, mode = "", 0, "exact"
     for _ in range(args.steps):
-        v, s, desc, threads, mode = cpu_sample(images=1)
+        v, s, desc, threads, mode = cpu_sample(images=1, wl=wl)
         vals.append(v)
         secs.append(s)
     value = statistics.median(vals)
@@ -217,7 +245,8 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 GEMMs, f32 softmax" if mode == "bf16" else "f32",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.5) rel-pos tables)",
-        "config": {"workload": "config 4 sample: SAM ViT-H attention, 1 image per step, 32 layers", "images_per_step": 1},
+        "config": {"workload": f"config {3 if args.config == 3 else 4} sample: {wl.name} attention, 1 image per step, "
+                               f"{wl.depth} layers", "images_per_step": 1},
         "images_per_s": 1.0 / statistics.median(secs),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -230,6 +259,120 @@ def run_reference(args):
 # GPU arm
 # --------------------------------------------------------------------------------------------
 
+def bind_to_gpu_numa_node(local_rank):
+    """Pin this process to the CPUs of its GPU's NUMA node, so that the pinned host buffers of the e2e leg
+    are first-touched there. Returns the node (None if the host reports none)."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        handle = pynvml.nvmlDeviceGetHandleByIndex(local_rank)
+        bus = pynvml.nvmlDeviceGetPciInfo(handle).busId
+        bus = bus.decode() if isinstance(bus, bytes) else bus
+        bus = bus.lower()[-12:]  # domain:bus:device.function as sysfs spells it
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return None
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            cpus = set()
+            for part in f.read().strip().split(","):
+                a, _, b = part.partition("-")
+                cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0) or cpus
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return node
+    except Exception:
+        return None
+
+
+class Step:
+    """The layers of one step of a workload, with inputs resident on the device (drawn in a fixed order from a
+    per-rank generator, so a rank's inputs and outputs do not depend on the world size)."""
+
+    def __init__(self, torch, lib, wl, images, device, rank, sptr, table_std=0.5):
+        self.lib, self.wl, self.images, self.sptr = lib, wl, images, sptr
+        self.geoms = layer_geoms(images, wl)
+        gen = torch.Generator(device=device).manual_seed(1000 + rank)
+
+        def rnd(*shape, std=1.0):
+            return (torch.randn(*shape, device=device, generator=gen) * std).to(torch.bfloat16)
+
+        hd = wl.hd
+        self.sets = {}
+        for kind in KINDS:
+            _, h, w, bh = next(g for g in self.geoms if g[0] == kind)
+            n = h * w
+            self.sets[kind] = dict(q=rnd(bh, n, hd), kt=rnd(bh, hd, n), v=rnd(bh, n, hd),
+                                   out=torch.empty(bh, n, hd, device=device, dtype=torch.bfloat16))
+        self.tables = [rnd(4 * h - 2, hd, std=table_std) for (_, h, w, _) in self.geoms]
+        self.scale = hd ** -0.5
+        self.flops = sum(layer_flops(h, w, bh, hd) for (_, h, w, bh) in self.geoms)
+
+    def launch(self, li, sets=None, stream_ptr=None):
+        kind, h, w, bh = self.geoms[li]
+        s = (sets or self.sets)[kind]
+        rc = self.lib.samrs_relpos_attn_fwd(s["q"].data_ptr(), s["kt"].data_ptr(), s["v"].data_ptr(),
+                                            self.tables[li].data_ptr(), s["out"].data_ptr(), bh, h, w, self.wl.hd,
+                                            self.scale, 2, stream_ptr or self.sptr)
+        if rc != 0:
+            raise RuntimeError(self.lib.samrs_last_error().decode())
+
+    def run(self):
+        for li in range(len(self.geoms)):
+            self.launch(li)
+
+    def checksums(self):
+        return [float(self.sets[k]["out"].float().sum().item()) for k in KINDS]
+
+
+def time_workload(torch, samrs, step, stream, dist, device, steps, warmup, per_launch=False, clocks=None):
+    """W untimed warm-up steps, then K steps timed with CUDA events on the launch stream between barriers;
+    returns (local ms, max-over-ranks ms, {kind: [per-launch ms]})."""
+    for _ in range(warmup):
+        step.run()
+    torch.cuda.synchronize()
+    if samrs.device_status() != 0:
+        raise RuntimeError("device status word set during warm-up")
+    depth = len(step.geoms)
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(depth)]
+          for _ in range(steps)] if per_launch else None
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.__enter__()
+    a.record(stream)
+    for k in range(steps):
+        for li in range(depth):
+            if per_launch:
+                ev[k][li][0].record(stream)
+            step.launch(li)
+            if per_launch:
+                ev[k][li][1].record(stream)
+    b.record(stream)
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.__exit__(None, None, None)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    local_ms = a.elapsed_time(b)
+    per_kind = {k: [] for k in KINDS}
+    if per_launch:
+        for k in range(steps):
+            for li in range(depth):
+                per_kind[step.geoms[li][0]].append(ev[k][li][0].elapsed_time(ev[k][li][1]))
+    return local_ms, max_over_ranks(local_ms, dist, device), per_kind
+
+
+def summary_line(step, world, steps, max_ms):
+    return {"value": step.flops * steps * world / (max_ms / 1e3) / 1e12, "unit": UNIT,
+            "images_per_s": step.images * world * steps / (max_ms / 1e3), "ms_per_step": max_ms / steps,
+            "images_per_gpu": step.images, "steps": steps}
+
+
 def run_ours(args):
     import torch
     samrs = importlib.import_module("sam-rs_b200")
@@ -238,6 +381,7 @@ def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    numa = bind_to_gpu_numa_node(local)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     dist = None
@@ -246,136 +390,113 @@ def run_ours(args):
         import torch.distributed as tdist
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
         dist = tdist
-
-    images = args.images
-    geoms = layer_geoms(images)
-    gen = torch.Generator(device=device).manual_seed(1000 + rank)
     stream = torch.cuda.current_stream(device)
     sptr = stream.cuda_stream
-
-    def rnd(*shape, std=1.0):
-        return (torch.randn(*shape, device=device, generator=gen) * std).to(torch.bfloat16)
-
-    sets = {}
-    for kind, h, w, bh in {(g[0], g[1], g[2], g[3]) for g in geoms}:
-        n = h * w
-        sets[kind] = dict(q=rnd(bh, n, HD), kt=rnd(bh, HD, n), v=rnd(bh, n, HD),
-                          out=torch.empty(bh, n, HD, device=device, dtype=torch.bfloat16))
-    tables = [rnd(4 * h - 2, HD, std=0.5) for (_, h, w, _) in geoms]
-    scale = HD ** -0.5
-
-    def launch(li):
-        kind, h, w, bh = geoms[li]
-        s = sets[kind]
-        rc = lib.samrs_relpos_attn_fwd(s["q"].data_ptr(), s["kt"].data_ptr(), s["v"].data_ptr(),
-                                       tables[li].data_ptr(), s["out"].data_ptr(), bh, h, w, HD, scale, 2, sptr)
-        if rc != 0:
-            raise RuntimeError(lib.samrs_last_error().decode())
-
-    for _ in range(args.warmup):
-        for li in range(DEPTH):
-            launch(li)
-    torch.cuda.synchronize()
-    if samrs.device_status() != 0:
-        raise RuntimeError("device status word set during warm-up")
-
-    K = args.steps
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(DEPTH)]
-          for _ in range(K)]
-    step_start = torch.cuda.Event(enable_timing=True)
-    step_end = torch.cuda.Event(enable_timing=True)
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        step_start.record(stream)
-        for k in range(K):
-            for li in range(DEPTH):
-                ev[k][li][0].record(stream)
-                launch(li)
-                ev[k][li][1].record(stream)
-        step_end.record(stream)
-        torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    local_ms = step_start.elapsed_time(step_end)
-    max_ms = max_over_ranks(local_ms, dist, device)
-    per_kind = {"global": [], "window": []}
-    for k in range(K):
-        for li in range(DEPTH):
-            per_kind[geoms[li][0]].append(ev[k][li][0].elapsed_time(ev[k][li][1]))
-    status = samrs.device_status()
-
-    flops_step = sum(layer_flops(h, w, bh) for (_, h, w, bh) in geoms)
-    total_flops = flops_step * K * world
-    value = total_flops / (max_ms / 1e3) / 1e12
-    ms_per_step = max_ms / K
-    images_per_s = images * world * K / (max_ms / 1e3)
-
-    # checksums of the last outputs, gathered to rank 0 (after timing)
-    csum = [float(sets["global"]["out"].float().sum().item()), float(sets["window"]["out"].float().sum().item())]
-    all_csum = gather_floats(csum + [local_ms, float(status)], dist, device)
-
     hbm, tf_burst, tf_sust, peak_src = load_peaks()
-    traffic = load_traffic()
+
+    if args.config == 5:
+        sweep = run_sweep(torch, samrs, lib, device, rank, sptr, stream, dist, world, args.steps, args.warmup)
+        if rank == 0:
+            best = max(sweep, key=lambda r: r["value"])
+            line = {"metric": METRIC, "value": best["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": best["ms_per_step"], "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                    "data": "synthetic (seeded N(0,1) activations, N(0,0.5) rel-pos tables)",
+                    "config": {"workload": "config 5: config 4 (" + CONFIGS[4].describe() + ") at 8-128 images per "
+                                           "GPU; value = the best point of the sweep", "parallelism": f"dp{world}"},
+                    "sweep": sweep, "gpu_launches": sum(36 * r["steps"] for r in sweep)}
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    wl = CONFIGS[args.config]
+    images = args.images or wl.images
+    step = Step(torch, lib, wl, images, device, rank, sptr)
+    K = args.steps
+    clk = ClockSampler(local)
+    samrs.recompute_count(clear=True)
+    local_ms, max_ms, per_kind = time_workload(torch, samrs, step, stream, dist, device, K, args.warmup,
+                                               per_launch=True, clocks=clk)
+    recomputed = samrs.recompute_count(clear=True)
+    status = samrs.device_status()
+    summ = summary_line(step, world, K, max_ms)
+
+    # checksums of the last outputs and per-rank status, gathered to rank 0 (after timing)
+    all_csum = gather_floats(step.checksums() + [local_ms, float(status)], dist, device)
+    traffic = load_traffic() if args.config == 4 else {}
 
     def roof(kind):
-        _, h, w, bh = next(g for g in geoms if g[0] == kind)
+        _, h, w, bh = next(g for g in step.geoms if g[0] == kind)
         avg_ms = statistics.mean(per_kind[kind])
         if kind == "global":
-            ach = layer_flops(h, w, bh) / (avg_ms / 1e3) / 1e12
+            ach = layer_flops(h, w, bh, wl.hd) / (avg_ms / 1e3) / 1e12
             peak = tf_burst
             r = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                  "peak_source": f"{peak_src} bf16 burst (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback"}
         else:
-            ach = layer_bytes(h, w, bh) / (avg_ms / 1e3) / 1e9
+            ach = layer_bytes(h, w, bh, wl.hd) / (avg_ms / 1e3) / 1e9
             peak = hbm
             r = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
                  "peak_source": f"{peak_src} HBM copy (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback"}
         r["traffic"] = traffic.get(kind)
-        r["kernel"] = f"relpos_attn ({kind}, h={h} w={w} bh={bh} hd={HD})" + (
+        r["kernel"] = f"relpos_attn ({kind}, h={h} w={w} bh={bh} hd={wl.hd})" + (
             "; time of the single-pass kernel and its fixup launch together" if kind == "global" else "")
         r["avg_launch_ms"] = avg_ms
         r["launches"] = len(per_kind[kind])
         r["time_share"] = sum(per_kind[kind]) / sum(sum(v) for v in per_kind.values())
         return r
 
-    roofs = {k: roof(k) for k in ("global", "window")}
+    roofs = {k: roof(k) for k in KINDS}
     dominant = max(roofs, key=lambda k: roofs[k]["time_share"])
+    n_global = sum(1 for g in step.geoms if g[0] == "global")
+    global_ctas = (K + args.warmup) * n_global * step.geoms[wl.global_layers[0]][3] * 16  # warm-up steps count too
 
-    neighbours = run_neighbours(samrs, lib, images, device, sptr, hbm) if not args.no_neighbours else None
+    extra = {}
+    if args.config == 4 and not args.no_configs:
+        extra["3"] = run_config3(torch, samrs, lib, device, rank, sptr, stream, dist, world, min(K, 5), args.warmup)
+        extra["5"] = run_sweep(torch, samrs, lib, device, rank, sptr, stream, dist, world, min(K, 5), args.warmup)
+        extra["recompute_by_table_std"] = recompute_rates(torch, samrs, lib, device, sptr)
+
+    neighbours = run_neighbours(samrs, lib, images, device, sptr, hbm, wl) \
+        if not args.no_neighbours and args.config == 4 else None
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world)
+        e2e = run_e2e(args, samrs, step, device, stream, dist, world, max_ms / K)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        v, s, desc, threads, _ = cpu_sample(images=1)
+        v, s, desc, threads, _ = cpu_sample(images=1, wl=wl)
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
-            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, N(0,0.5) rel-pos tables)",
-            "config": {"workload": "config 4: SAM ViT-H encoder attention (rel-pos), bf16, 32 layers "
-                                   "(global 7,15,23,31 / windowed 14x14), head_dim 80, 16 heads",
+            "metric": METRIC, "value": summ["value"], "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": summ["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.5) rel-pos tables)",
+            "config": {"workload": f"config {args.config}: " + wl.describe(),
                        "images_per_gpu": images, "global_batch": images * world, "parallelism": f"dp{world}",
-                       "l2": "no flush; every launch's inputs (>= 1 GB) exceed the 126 MB L2"},
-            "images_per_s": images_per_s,
-            "tflops_by_layer": {k: layer_flops(*next(g for g in geoms if g[0] == k)[1:]) /
-                                (statistics.mean(per_kind[k]) / 1e3) / 1e12 for k in per_kind},
+                       "l2": "no flush; every launch's inputs (>= 0.3 GB) exceed the 126 MB L2"},
+            "images_per_s": summ["images_per_s"],
+            "tflops_by_layer": {k: layer_flops(*next(g for g in step.geoms if g[0] == k)[1:], wl.hd) /
+                                (statistics.mean(per_kind[k]) / 1e3) / 1e12 for k in KINDS},
             "roofline": roofs[dominant],
             "roofline_other": roofs["window" if dominant == "global" else "global"],
             # a bf16 global layer is two launches: the single-pass kernel and the fixup of the CTAs it marked
-            "gpu_launches": K * sum(2 if g[0] == "global" else 1 for g in geoms),
+            "gpu_launches": K * sum(2 if g[0] == "global" else 1 for g in step.geoms),
+            "recomputed_global_ctas": {"ctas": recomputed, "of": global_ctas,
+                                       "fraction": recomputed / global_ctas if global_ctas else 0.0},
             "clocks": clk.summary(),
             "device_status": [int(c[-1]) for c in all_csum],
             "rank_ms": [c[-2] for c in all_csum],
             "checksums": [c[:2] for c in all_csum],
+            "numa_node": numa,
         }
+        if extra:
+            line["configs"] = extra
         if cpu is not None:
             line["cpu_baseline"] = cpu
         if e2e is not None:
@@ -389,28 +510,81 @@ def run_ours(args):
     return 0
 
 
-def run_neighbours(samrs, lib, images, device, sptr, hbm, reps=10):
+def run_config3(torch, samrs, lib, device, rank, sptr, stream, dist, world, steps, warmup):
+    """BASELINE config 3 (ViT-L, 16 images per GPU, hd 64, 24 layers), timed like the headline."""
+    step = Step(torch, lib, CONFIGS[3], CONFIGS[3].images, device, rank, sptr)
+    _, max_ms, per_kind = time_workload(torch, samrs, step, stream, dist, device, steps, warmup, per_launch=True)
+    out = summary_line(step, world, steps, max_ms)
+    out["workload"] = "config 3: " + CONFIGS[3].describe()
+    for kind in KINDS:
+        _, h, w, bh = next(g for g in step.geoms if g[0] == kind)
+        ms = statistics.mean(per_kind[kind])
+        out[f"{kind}_ms"] = ms
+        out[f"{kind}_tflops"] = layer_flops(h, w, bh, 64) / (ms / 1e3) / 1e12
+        out[f"{kind}_gbs"] = layer_bytes(h, w, bh, 64) / (ms / 1e3) / 1e9
+    out["checksums_rank0"] = step.checksums() if rank == 0 else None
+    del step
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_sweep(torch, samrs, lib, device, rank, sptr, stream, dist, world, steps, warmup):
+    """config 4 at 8, 16, 32, 64 and 128 images per GPU."""
+    rows = []
+    for images in SWEEP_IMAGES:
+        step = Step(torch, lib, CONFIGS[4], images, device, rank, sptr)
+        _, max_ms, _ = time_workload(torch, samrs, step, stream, dist, device, steps, warmup)
+        rows.append(summary_line(step, world, steps, max_ms))
+        del step
+        torch.cuda.empty_cache()
+    return rows
+
+
+def recompute_rates(torch, samrs, lib, device, sptr, images=8):
+    """Share of bf16 global-layer CTAs the exact second pass recomputes, by rel-pos table std (activations
+    N(0,1)), and one case with activations N(0,2) as well."""
+    out = {}
+    gen = torch.Generator(device=device).manual_seed(77)
+    bh, n, hd = images * 16, 4096, HD
+    for label, a_std, t_std in (("t0.5", 1.0, 0.5), ("t1", 1.0, 1.0), ("t2", 1.0, 2.0), ("t2_a2", 2.0, 2.0)):
+        q = (torch.randn(bh, n, hd, device=device, generator=gen) * a_std).bfloat16()
+        kt = (torch.randn(bh, hd, n, device=device, generator=gen) * a_std).bfloat16()
+        v = torch.randn(bh, n, hd, device=device, generator=gen).bfloat16()
+        t = (torch.randn(254, hd, device=device, generator=gen) * t_std).bfloat16()
+        o = torch.empty_like(q)
+        samrs.recompute_count(clear=True)
+        rc = lib.samrs_relpos_attn_fwd(q.data_ptr(), kt.data_ptr(), v.data_ptr(), t.data_ptr(), o.data_ptr(), bh, 64,
+                                       64, hd, hd ** -0.5, 2, sptr)
+        if rc != 0:
+            raise RuntimeError(lib.samrs_last_error().decode())
+        out[label] = samrs.recompute_count(clear=True) / (bh * 16)
+    return out
+
+
+def run_neighbours(samrs, lib, images, device, sptr, hbm, wl, reps=10):
     """The path's neighbours on the token grid at the bench workload (not part of the metric): the qkv
     split fused with the window partition and the head merge fused with the unpartition, for the windowed
     (ws 14, pad 64 -> 70) and the global (one 64x64 window) layers. Algorithmic bytes: the real tokens'
     y (3C) read and q, kt, v (pads included) written; the real tokens' attention rows read and written."""
     import torch
-    nh, c, es = 16, 16 * HD, 2
+    nh, hd, es = wl.heads, wl.hd, 2
+    c = nh * hd
     out = {}
-    y = (torch.randn(images * 4096, 3 * c, device=device) * 0.5).to(torch.bfloat16)
-    bias = (torch.randn(3 * c, device=device) * 0.1).to(torch.bfloat16)
+    gen = torch.Generator(device=device).manual_seed(5)
+    y = (torch.randn(images * 4096, 3 * c, device=device, generator=gen) * 0.5).to(torch.bfloat16)
+    bias = (torch.randn(3 * c, device=device, generator=gen) * 0.1).to(torch.bfloat16)
     for name, ws in (("window", 14), ("global", 0)):
         n, nwin = (196, 25) if ws else (4096, 1)
         bh = images * nwin * nh
-        packed = torch.empty(3 * bh * n * HD, device=device, dtype=torch.bfloat16)
-        attn = torch.empty(bh, n, HD, device=device, dtype=torch.bfloat16)
+        packed = torch.empty(3 * bh * n * hd, device=device, dtype=torch.bfloat16)
+        attn = torch.empty(bh, n, hd, device=device, dtype=torch.bfloat16)
         merged = torch.empty(images * 4096, c, device=device, dtype=torch.bfloat16)
         calls = {
             "qkv_split_window": (lambda: lib.samrs_qkv_split_window_fwd(
-                y.data_ptr(), bias.data_ptr(), packed.data_ptr(), images, 64, 64, ws, nh, HD, 2, sptr),
-                images * 4096 * 3 * c * es + 3 * bh * n * HD * es),
+                y.data_ptr(), bias.data_ptr(), packed.data_ptr(), images, 64, 64, ws, nh, hd, 2, sptr),
+                images * 4096 * 3 * c * es + 3 * bh * n * hd * es),
             "window_merge": (lambda: lib.samrs_window_merge_fwd(
-                attn.data_ptr(), merged.data_ptr(), images, 64, 64, ws, nh, HD, 2, sptr),
+                attn.data_ptr(), merged.data_ptr(), images, 64, 64, ws, nh, hd, 2, sptr),
                 2 * images * 4096 * c * es),
         }
         for kname, (fn, nbytes) in calls.items():
@@ -433,16 +607,50 @@ def run_neighbours(samrs, lib, images, device, sptr, hbm, reps=10):
     return out
 
 
-def run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world):
+def copy_bandwidth(torch, device, dist, nbytes=1 << 30, reps=4):
+    """Measured pinned host <-> device copy bandwidth of this rank (GB/s), with every rank copying at the same
+    time (the host side is shared): one cudaMemcpyAsync per buffer, H2D and D2H each alone, then both at once
+    on two streams (the e2e leg overlaps them)."""
+    host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    host2 = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    dev2 = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    s1, s2 = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    res = {}
+    for name in ("h2d", "d2h", "both"):
+        dev.copy_(host, non_blocking=True)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            if name in ("h2d", "both"):
+                with torch.cuda.stream(s1):
+                    dev.copy_(host, non_blocking=True)
+            if name in ("d2h", "both"):
+                with torch.cuda.stream(s2):
+                    host2.copy_(dev2, non_blocking=True)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        res[name] = nbytes * reps * (2 if name == "both" else 1) / dt / 1e9
+    del host, host2, dev, dev2
+    return res
+
+
+def run_e2e(args, samrs, step, device, stream, dist, world, device_ms_per_step):
     """Same workload through the C ABI with host (pinned) buffers: every layer copies its q, kt, v
     host->device, runs the op, and copies its output device->host, all inside the timed region.
     Serving-style pipelining: two device buffer sets per layer kind and three streams (upload, compute,
     download) ordered by events, so layer l+1's upload, layer l's kernel and layer l-1's download overlap
-    (PCIe is full duplex)."""
+    (PCIe is full duplex). The roofline of this leg is the host link: the measured pinned-copy bandwidth
+    of the box at this world size."""
     import torch
+    sets = step.sets
     host = {}
     dev = {}
-    for kind, s in sets.items():
+    for kind in KINDS:
+        s = sets[kind]
         host[kind] = {k: torch.empty(s[k].shape, dtype=s[k].dtype, pin_memory=True) for k in ("q", "kt", "v", "out")}
         for k in ("q", "kt", "v"):
             host[kind][k].copy_(s[k])
@@ -450,17 +658,16 @@ def run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world):
     torch.cuda.synchronize()
     s_up, s_down = torch.cuda.Stream(device), torch.cuda.Stream(device)
     sptr = stream.cuda_stream
-    scale = HD ** -0.5
     # per (kind, buffer): the compute that last read the inputs / wrote the output, the download of it
-    comp_done = {k: [None, None] for k in sets}
-    down_done = {k: [None, None] for k in sets}
+    comp_done = {k: [None, None] for k in KINDS}
+    down_done = {k: [None, None] for k in KINDS}
     h2d = d2h = 0
 
-    def step():
+    def one_step():
         nonlocal h2d, d2h
         h2d = d2h = 0
-        use = {k: 0 for k in sets}
-        for li, (kind, h, w, bh) in enumerate(geoms):
+        use = {k: 0 for k in KINDS}
+        for li, (kind, h, w, bh) in enumerate(step.geoms):
             bi = use[kind] & 1
             use[kind] += 1
             d, hb = dev[kind][bi], host[kind]
@@ -475,10 +682,7 @@ def run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world):
             stream.wait_event(up)
             if down_done[kind][bi] is not None:
                 stream.wait_event(down_done[kind][bi])  # the previous output in this set is on the host
-            rc = lib.samrs_relpos_attn_fwd(d["q"].data_ptr(), d["kt"].data_ptr(), d["v"].data_ptr(),
-                                           tables[li].data_ptr(), d["out"].data_ptr(), bh, h, w, HD, scale, 2, sptr)
-            if rc != 0:
-                raise RuntimeError(lib.samrs_last_error().decode())
+            step.launch(li, sets={kind: d}, stream_ptr=sptr)
             cd = torch.cuda.Event()
             cd.record(stream)
             comp_done[kind][bi] = cd
@@ -497,7 +701,7 @@ def run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world):
             e.record(st)
             stream.wait_event(e)
 
-    step()
+    one_step()
     join()
     torch.cuda.synchronize()
     k = max(1, min(args.steps, args.e2e_steps))
@@ -510,14 +714,27 @@ def run_e2e(args, samrs, lib, geoms, sets, tables, device, stream, dist, world):
     s_up.wait_event(a)
     s_down.wait_event(a)
     for _ in range(k):
-        step()
+        one_step()
     join()
     b.record(stream)
     torch.cuda.synchronize()
-    ms = max_over_ranks(a.elapsed_time(b), dist, device)
-    flops = sum(layer_flops(h, w, bh) for (_, h, w, bh) in geoms) * k * world
-    return {"value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": k, "ms_per_step": ms / k,
+    local_ms = a.elapsed_time(b)
+    ms = max_over_ranks(local_ms, dist, device)
+    del host, dev
+    torch.cuda.empty_cache()
+    bw = copy_bandwidth(torch, device, dist)
+    bw_min = {kname: max_over_ranks(-v, dist, device) * -1 for kname, v in bw.items()}  # slowest rank
+    step_s = local_ms / k / 1e3
+    # the host-link bound of one step: uploads and downloads overlap (full duplex), and neither beats the
+    # measured copy rates; the device compute is the third term
+    bound_s = max(h2d / (bw_min["h2d"] * 1e9), d2h / (bw_min["d2h"] * 1e9), (h2d + d2h) / (bw_min["both"] * 1e9),
+                  device_ms_per_step / 1e3)
+    return {"value": step.flops * k * world / (ms / 1e3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": k, "ms_per_step": ms / k,
+            "h2d_gbs": h2d / step_s / 1e9, "d2h_gbs": d2h / step_s / 1e9,
+            "copy_gbs_measured": bw_min,
+            "roofline": {"bound": "host link (pinned cudaMemcpyAsync, all ranks at once)", "bound_ms_per_step":
+                         bound_s * 1e3, "frac": bound_s / (ms / k / 1e3)},
             "path": "C ABI samrs_relpos_attn_fwd, pinned host buffers, upload/compute/download streams"}
 
 
@@ -527,10 +744,12 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--images", type=int, default=32, help="images per GPU (config 4: 32)")
+    ap.add_argument("--config", type=int, choices=[3, 4, 5], default=4)
+    ap.add_argument("--images", type=int, default=0, help="images per GPU (default: the config's, 32 for config 4)")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip configs 3 and 5 in the default config-4 run")
     ap.add_argument("--no-neighbours", action="store_true", help="skip timing the qkv split / head merge kernels")
     args = ap.parse_args(argv)
     if args.warmup < 3:

@@ -133,8 +133,29 @@ SAMRS_API int samrs_abi_version(void);
  * fails, records a code here and the kernel returns early. samrs_device_status synchronises
  * `stream`, returns the word of the current device (0 = healthy) and clears it when `clear` != 0.
  * Codes: 1 = mbarrier/TMA wait timed out, 2 = MMA wait timed out, 3 = bad launch geometry.
+ * While the word is nonzero every tensor-core kernel of the device returns at entry without writing
+ * its output: the outputs of the call that reported and of every later call are undefined until the
+ * word is cleared. Once samrs_device_status has read a nonzero word without clearing it, every other
+ * entry point on that device returns SAMRS_ERR_DEVICE (no launch) until a call with `clear` != 0.
+ * Callers poll it where they synchronise anyway (sam-rs: `Sam::sync`, src/model.rs:121-124).
+ * No counterpart in the reference (its kernels cannot wait on anything).
  */
 SAMRS_API int samrs_device_status(void* stream, int clear);
+
+/*
+ * Number of bf16 global-layer CTAs (one head x 256 query rows) that were recomputed by the exact second
+ * pass since the last clear (the single-pass bf16 kernel hands a CTA to it when a row's softmax weights
+ * left the range it keeps them in). Synchronises `stream`; `clear` != 0 resets the count.
+ * A diagnostic with no counterpart in the reference.
+ */
+SAMRS_API int samrs_recompute_count(void* stream, int64_t* count, int clear);
+
+/*
+ * Self-test hook of the library's own exp2 polynomial (the FMA-pipe exponential the windowed kernel uses
+ * for one key pair in four): y_poly[i] = the polynomial at x[i], y_lib[i] = CUDA's exp2f(x[i]); device
+ * f32 buffers of n elements. Test infrastructure; no counterpart in the reference.
+ */
+SAMRS_API int samrs_selftest_ex2(const void* x, void* y_poly, void* y_lib, int64_t n, void* stream);
 
 #ifdef __cplusplus
 }

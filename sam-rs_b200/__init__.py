@@ -14,6 +14,7 @@ Every op runs a CUDA kernel of this package; a tensor that is not a contiguous C
 f32/f16/bf16 raises, as the reference's `bail!` does (src/kernels.rs:1092,1097-1102). There is no
 CPU fallback: if libsamrs_b200.so is missing, the first op call raises.
 """
+import ctypes
 import math
 
 import torch
@@ -23,7 +24,7 @@ from ._abi import SamrsError
 
 __all__ = ["relpos_softmax", "attention_relpos", "attention_relpos_cpu", "qkv_split", "qkv_split_window",
            "window_merge", "bmm", "Attention", "window_partition", "window_unpartition", "device_status",
-           "SamrsError"]
+           "recompute_count", "SamrsError"]
 
 _DTYPES = {torch.float32: _abi.F32, torch.float16: _abi.F16, torch.bfloat16: _abi.BF16}
 _IMPLS = {"auto": _abi.IMPL_AUTO, "simt": _abi.IMPL_SIMT, "tc": _abi.IMPL_TC}
@@ -166,6 +167,14 @@ def device_status(clear=True):
     if rc < 0:
         raise SamrsError(rc, _abi.lib().samrs_last_error().decode())
     return rc
+
+
+def recompute_count(clear=True):
+    """Synchronise the current stream and return how many bf16 global-layer CTAs (one head x 256 query rows)
+    the exact second pass recomputed since the last clear."""
+    n = ctypes.c_int64(0)
+    _abi.check(_abi.lib().samrs_recompute_count(_stream(), ctypes.byref(n), 1 if clear else 0))
+    return int(n.value)
 
 
 def window_partition(x, ws):

@@ -23,6 +23,10 @@ __device__ unsigned int g_status = 0;
 
 __device__ __forceinline__ void report(unsigned int code) { atomicCAS(&g_status, 0u, code); }
 
+// Number of bf16 global-layer CTAs (one head x 256 query rows) that the exact fixup launch recomputed,
+// read and cleared by samrs_recompute_count(). A statistic for the caller, not read by any kernel.
+__device__ unsigned long long g_recomputed = 0;
+
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }

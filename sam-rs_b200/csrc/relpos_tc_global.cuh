@@ -236,17 +236,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* rhmax_park = reinterpret_cast<float*>(smem + L::OFF_RHMAX);
   volatile int* abort_flag = &bars->abort_flag;
 
-  if (device_faulted()) return;  // an earlier CTA reported a fault: do no more work
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long bh = blockIdx.x / (kN / 256);
   const int ct = blockIdx.x % (kN / 256);
   const int row0 = ct * 256;  // first query row of the CTA
   const int I0 = ct * 4;      // its first grid row
   T* const marker = out + (bh * kN + row0) * HD;  // first element of the CTA's output block
-  if constexpr (MODE == kModeFixup) {
-    // only CTAs whose speculative pass left the NaN marker (the same value for every thread)
-    const float m = to_f(*reinterpret_cast<volatile T*>(marker));
-    if (!(m != m)) return;
+  {
+    // The whole CTA leaves here or none of it does (thread 0 decides; the barriers, TMEM and the warp
+    // roles below need every warp): after an earlier CTA reported a fault, and in the fixup launch for the
+    // CTAs whose speculative pass did not leave the NaN marker.
+    int skip = 0;
+    if (threadIdx.x == 0) {
+      skip = device_faulted();
+      if constexpr (MODE == kModeFixup) {
+        const float m = to_f(*reinterpret_cast<volatile T*>(marker));
+        skip |= !(m != m);
+        if (!skip) atomicAdd(&g_recomputed, 1ull);
+      }
+    }
+    if (__syncthreads_or(skip)) return;
   }
 
   if (threadIdx.x == 0) {

@@ -314,7 +314,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   using namespace sm100;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
-  if (device_faulted()) return;
+  // After an earlier CTA reported a fault the whole CTA leaves, together (thread 0 decides: the barriers,
+  // TMEM and the warp roles below need every warp).
+  if (__syncthreads_or(threadIdx.x == 0 && device_faulted())) return;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + L::OFF_BAR);
   volatile int* abort_flag = &bars->abort_flag;

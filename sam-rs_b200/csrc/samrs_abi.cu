@@ -5,6 +5,8 @@
 #include <stdarg.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <stdint.h>
 #include <stdio.h>
 
@@ -43,31 +45,43 @@ size_t elem_size(int dtype) { return dtype == SAMRS_F32 ? 4 : 2; }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// Per-device cache of "is this an sm_100 device" and the opt-in shared memory limit.
+// Per-device cache of "is this an sm_100 device", the opt-in shared memory limit and the SM count,
+// filled once per device (std::call_once: entry points may run on several host threads at once).
 struct DevInfo {
-  int checked = 0;
   int is_sm100 = 0;
   int max_smem_optin = 0;
   int num_sms = 0;
 };
-DevInfo g_dev[64];
+constexpr int kMaxDevices = 64;
+DevInfo g_dev[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+// Host-side record of a nonzero device status word: set when samrs_device_status reads a nonzero word
+// without clearing it, reset when it clears the word. While it is set every entry point of that device
+// returns SAMRS_ERR_DEVICE instead of launching.
+std::atomic<unsigned int> g_fault_seen[kMaxDevices];
 
-int device_info(DevInfo** out) {
+int device_info(DevInfo** out, int* dev_out = nullptr) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(SAMRS_ERR_NODEVICE, "no CUDA device is current");
   DevInfo& d = g_dev[dev];
-  if (!d.checked) {
+  std::call_once(g_dev_once[dev], [&d, dev]() {
     int major = 0, minor = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
     cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
     d.is_sm100 = (major == 10 && minor == 0);
-    d.checked = 1;
-  }
+  });
   if (!d.is_sm100) return fail(SAMRS_ERR_NODEVICE, "this library is built for sm_100a (B200) only");
+  const unsigned int seen = g_fault_seen[dev].load(std::memory_order_relaxed);
+  if (seen)
+    return fail(SAMRS_ERR_DEVICE,
+                "device status word is %u (a kernel reported a fault; kernels are no-ops until "
+                "samrs_device_status(stream, 1) clears it)",
+                seen);
   *out = &d;
+  if (dev_out) *dev_out = dev;
   return SAMRS_OK;
 }
 
@@ -195,6 +209,24 @@ int launch_merge(const void* attn, void* out, int64_t images, const WinGeom& g, 
   else
     window_merge_kernel<T, 1, uint64_t><<<(unsigned)blocks, 256, 0, st>>>(ap, op, (long)images, g);
   return launch_status("window_merge");
+}
+
+// Test hook of the windowed kernel's exp2 polynomial (sm100::ex2_poly2): y_poly = the polynomial, y_lib =
+// CUDA's exp2f, for the same x (pairs (2i, 2i+1), as the kernel evaluates them).
+__global__ void selftest_ex2_kernel(const float* __restrict__ x, float* __restrict__ y_poly, float* __restrict__ y_lib,
+                                    int64_t n) {
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; 2 * p < n; p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = 2 * p;
+    const bool two = i + 1 < n;
+    const float2 xv = make_float2(x[i], two ? x[i + 1] : 0.f);
+    const float2 yv = sm100::ex2_poly2(xv);
+    y_poly[i] = yv.x;
+    y_lib[i] = exp2f(xv.x);
+    if (two) {
+      y_poly[i + 1] = yv.y;
+      y_lib[i + 1] = exp2f(xv.y);
+    }
+  }
 }
 
 }  // namespace
@@ -344,6 +376,9 @@ int samrs_window_merge_fwd(const void* attn, void* out, int64_t images, int h, i
 }
 
 int samrs_device_status(void* stream, int clear) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(SAMRS_ERR_NODEVICE, "no CUDA device is current");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "device_status: stream sync failed: %s", cudaGetErrorString(e));
@@ -355,7 +390,39 @@ int samrs_device_status(void* stream, int clear) {
     e = cudaMemcpyToSymbol(samrs::g_status, &zero, sizeof(zero));
     if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "device_status: clear failed: %s", cudaGetErrorString(e));
   }
+  g_fault_seen[dev].store(clear ? 0u : word, std::memory_order_relaxed);
   return (int)word;
+}
+
+int samrs_recompute_count(void* stream, int64_t* count, int clear) {
+  if (!count) return fail(SAMRS_ERR_INVALID, "recompute_count: null output pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "recompute_count: stream sync failed: %s", cudaGetErrorString(e));
+  unsigned long long v = 0;
+  e = cudaMemcpyFromSymbol(&v, samrs::g_recomputed, sizeof(v));
+  if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "recompute_count: read failed: %s", cudaGetErrorString(e));
+  if (clear) {
+    const unsigned long long zero = 0;
+    e = cudaMemcpyToSymbol(samrs::g_recomputed, &zero, sizeof(zero));
+    if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "recompute_count: clear failed: %s", cudaGetErrorString(e));
+  }
+  *count = (int64_t)v;
+  return ok();
+}
+
+int samrs_selftest_ex2(const void* x, void* y_poly, void* y_lib, int64_t n, void* stream) {
+  if (n < 0 || n > ((int64_t)1 << 30)) return fail(SAMRS_ERR_INVALID, "selftest_ex2: n = %lld", (long long)n);
+  if (n == 0) return ok();
+  if (!x || !y_poly || !y_lib) return fail(SAMRS_ERR_INVALID, "selftest_ex2: null pointer");
+  DevInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  const int64_t pairs = (n + 1) / 2;
+  const unsigned blocks = (unsigned)std::min<int64_t>((pairs + 255) / 256, (int64_t)dev->num_sms * 8);
+  selftest_ex2_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const float*>(x), static_cast<float*>(y_poly), static_cast<float*>(y_lib), n);
+  return launch_status("selftest_ex2");
 }
 
 }  // extern "C"

@@ -90,10 +90,13 @@ def test_config1_full_size_f32(samrs, cuda):
         assert err < F32_TOL, (h, err)
 
 
-@pytest.mark.parametrize("h,w,bh,hd", [(64, 64, 512, 80), (14, 14, 12800, 80)])
-def test_vith_full_batch_properties(samrs, cuda, h, w, bh, hd):
-    """Config 4 (ViT-H, B=32) at full size: linearity in v, convex-combination bounds, sampled heads vs oracle."""
-    g = torch.Generator(device=cuda).manual_seed(1234 + h)
+@pytest.mark.parametrize("h,w,bh,hd", [(64, 64, 512, 80), (14, 14, 12800, 80), (64, 64, 256, 64), (14, 14, 6400, 64)],
+                         ids=["config4-global", "config4-window", "config3-global", "config3-window"])
+def test_full_batch_properties(samrs, cuda, h, w, bh, hd):
+    """BASELINE configs 4 (ViT-H, 32 images: 16 heads, hd 80) and 3 (ViT-L, 16 images: 16 heads, hd 64) at full
+    size, bf16: linearity in v and convex-combination bounds over every head, and the oracle on heads sampled
+    evenly over the whole batch (32 per global layer, 64 per windowed layer)."""
+    g = torch.Generator(device=cuda).manual_seed(1234 + h + hd)
     n = h * w
     q = torch.randn(bh, n, hd, device=cuda, generator=g).bfloat16()
     kt = torch.randn(bh, hd, n, device=cuda, generator=g).bfloat16()
@@ -113,11 +116,11 @@ def test_vith_full_batch_properties(samrs, cuda, h, w, bh, hd):
     vmin = v1.float().amin(dim=1, keepdim=True)
     slack = 1e-2 * vmax.abs().clamp(min=1)
     assert bool(((o1.float() <= vmax + slack) & (o1.float() >= vmin - slack)).all())
-    for b in (0, bh // 2 + 1, bh - 1):
-        ref = oracle.attention_relpos(rounded(q[b:b + 1]), rounded(kt[b:b + 1]), rounded(v1[b:b + 1]), rounded(t),
-                                      h, w, scale)
-        err = excess_err(o1[b:b + 1].float().cpu().numpy(), ref, "bf16")
-        assert err < HALF_TOL, (b, err)
+    heads = np.unique(np.linspace(0, bh - 1, 32 if h == 64 else 64).round().astype(int))
+    idx = torch.from_numpy(heads).to(cuda)
+    ref = oracle.attention_relpos(rounded(q[idx]), rounded(kt[idx]), rounded(v1[idx]), rounded(t), h, w, scale)
+    err = parity_err(o1[idx].float().cpu().numpy(), ref, "bf16")
+    assert err < HALF_TOL, err
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
@@ -194,6 +197,46 @@ def test_global_bf16_overflow_recompute(samrs, cuda, hd):
     ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, w, scale)
     err = parity_err(got, ref, "bf16")
     assert err < HALF_TOL, err
+
+
+def test_bf16_recompute_counter(samrs, cuda):
+    """The recompute counter: random N(0,1) activations and N(0,0.5) tables need no exact second pass; the
+    overflow case above marks some CTAs (one head x 256 rows each) and the counter sees them."""
+    samrs.recompute_count(clear=True)
+    q, kt, v, t = make_inputs(64, 64, 4, 80, seed=3, table_std=0.5)
+    samrs.attention_relpos(*(to_dev(x, "bf16", cuda) for x in (q, kt, v, t)), 64, 64, 80 ** -0.5)
+    assert samrs.recompute_count() == 0
+    q, kt, v, t = make_inputs(64, 64, 2, 80, seed=91, table_std=0.5)
+    q[:, :, 0] = 4.0
+    v *= 1e35
+    kt[0, 0, 128 * 5 + 17] = 40.0
+    samrs.attention_relpos(*(to_dev(x, "bf16", cuda) for x in (q, kt, v, t)), 64, 64, 80 ** -0.5)
+    assert samrs.device_status() == 0
+    assert 1 <= samrs.recompute_count() <= 2 * 16
+
+
+def test_ex2_polynomial_against_cuda_exp2f(samrs, cuda):
+    """The windowed kernel's own exp2 (range reduction to [-1/2, 1/2] by rounding, degree-4 polynomial fitted
+    to relative error, exponent-field insertion) against CUDA's exp2f: relative error <= 3e-6 on [-120, 127];
+    below -120 the argument is clamped, so the result is 2^-120 (within the same relative error)."""
+    x = torch.cat([torch.linspace(-120.0, 127.0, 1 << 20, device=cuda),
+                   torch.rand(1 << 20, device=cuda) * 247.0 - 120.0,
+                   torch.arange(-120, 128, device=cuda, dtype=torch.float32),
+                   torch.arange(-120, 127, device=cuda, dtype=torch.float32) + 0.5]).contiguous()
+    yp, yl = torch.empty_like(x), torch.empty_like(x)
+    lib = samrs._abi.lib()
+    samrs._abi.check(lib.samrs_selftest_ex2(x.data_ptr(), yp.data_ptr(), yl.data_ptr(), x.numel(),
+                                            torch.cuda.current_stream().cuda_stream))
+    xd = x.double().cpu().numpy()
+    lib_rel = np.abs(yl.double().cpu().numpy() / np.exp2(xd) - 1).max()
+    assert lib_rel < 1e-6, lib_rel  # exp2f itself is within a couple of f32 ulps
+    rel = np.abs(yp.double().cpu().numpy() / yl.double().cpu().numpy() - 1).max()
+    assert rel <= 3e-6, rel
+    lo = torch.tensor([-121.0, -126.5, -150.0, -1e30], device=cuda)
+    ylo, ylo2 = torch.empty_like(lo), torch.empty_like(lo)
+    samrs._abi.check(lib.samrs_selftest_ex2(lo.data_ptr(), ylo.data_ptr(), ylo2.data_ptr(), lo.numel(),
+                                            torch.cuda.current_stream().cuda_stream))
+    assert np.abs(ylo.double().cpu().numpy() / 2.0 ** -120 - 1).max() <= 3e-6
 
 
 def test_tc_and_simt_agree_bf16(samrs, cuda):
