@@ -24,7 +24,7 @@
 // shared memory and written back by one bulk store per warp.
 //
 // Warps: 0 / 1 MMA issuers of query tile 1 / 0 (one warp each, so the two tiles' S -> softmax -> PV ->
-// epilogue chains never wait on each other), 2-3 kt loaders (thread 0 also issues the q TMA loads, the
+// epilogue chains never wait on each other; tile 1 starts half a step after tile 0), 2-3 kt loaders (thread 0 also issues the q TMA loads, the
 // last thread the v TMA loads; warp 2 allocates TMEM), 4-7 / 8-11 softmax + epilogue of query tile 0 / 1 (thread = query
 // row = TMEM lane); warp 11 covers rows 224..255 only, which are all padding, so it only keeps the
 // barrier counts.
@@ -379,9 +379,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ui = 0; ui < n_units && okk; ++ui) {
         const int s = ui & 1;
         const uint32_t ph = (ui >> 1) & 1;
-        // S_t(u) overwrites the tile's columns: the softmax warps must have read O_t(u-1)
+        // S_t(u) overwrites the tile's columns: the softmax warps must have read O_t(u-1). Tile 1's first S
+        // waits for tile 0's first softmax, which sets the two tiles half a step apart: one tile's softmax on
+        // the exp unit then overlaps the other's MMAs and epilogue instead of competing with its softmax.
         okk = wait(&bars->q_full[s], ph) && wait(&bars->k_full[s], ph) &&
-              (ui == 0 || wait(&bars->t_free[t], (ui - 1) & 1));
+              (ui == 0 ? (t == 0 || wait(&bars->p_full[0], 0)) : wait(&bars->t_free[t], (ui - 1) & 1));
         if (!okk) break;
         tc_fence_after();
 #pragma unroll
