@@ -10,10 +10,12 @@ layers in encoder order (src/sam1/encoder.rs:19-23), bf16:
         481.3 GFLOP per image, 15.40 TFLOP per step per GPU (4*N^2*hd per head: QK^T + PV)
     config 3: ViT-L, 16 images per GPU, 16 heads, head_dim 64, 24 layers, global at 5, 11, 17, 23
     config 5: config 4 swept over 8, 16, 32, 64 and 128 images per GPU
-The default run prints the config-4 line and carries configs 3 and 5 (shorter timings of the same kind) in
-its "configs" object; --config 3 / 5 print their own line.
+    config 2: the whole ViT-B encoder block stack (LayerNorm, the qkv / proj / MLP GEMMs with their fused
+        epilogues, the attention), f16, 8 images per GPU, 12 blocks
+The default run prints the config-4 line and carries configs 2, 3 and 5 (shorter timings) in its "configs"
+object, and the block's GEMMs at the ViT-H shapes in "gemms"; --config 2 / 3 / 5 print their own line.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 3|4|5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N   (one rank per GPU)
 
 Multi-GPU: the image batch is sharded (the per-GPU image count is fixed, weak scaling); there is no collective
@@ -59,6 +61,8 @@ class Workload:
 VIT_H = dict(name="SAM ViT-H", heads=16, hd=80, depth=32, global_layers=(7, 15, 23, 31))
 VIT_L = dict(name="SAM ViT-L", heads=16, hd=64, depth=24, global_layers=(5, 11, 17, 23))
 CONFIGS = {3: Workload(images=16, **VIT_L), 4: Workload(images=32, **VIT_H)}
+# config 2: the whole ViT-B block stack (src/sam1/encoder.rs:19-23 VIT_B, Block::forward :115-129), f16
+VIT_B_STACK = dict(images=8, c=768, heads=12, depth=12, global_layers=(2, 5, 8, 11), window=14)
 SWEEP_IMAGES = (8, 16, 32, 64, 128)  # config 5: config 4 at these images per GPU
 HD = VIT_H["hd"]
 
@@ -394,6 +398,23 @@ def run_ours(args):
     sptr = stream.cuda_stream
     hbm, tf_burst, tf_sust, peak_src = load_peaks()
 
+    if args.config == 2:
+        c2 = run_config2(torch, samrs, device, rank, dist, world, args.steps, args.warmup, stream)
+        if rank == 0:
+            line = {"metric": METRIC, "value": c2["tflops"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": c2["ms_per_step"], "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                    "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, N(0,0.5) rel-pos tables)",
+                    "config": {"workload": c2["workload"], "images_per_gpu": c2["images_per_gpu"],
+                               "parallelism": f"dp{world}"},
+                    "images_per_s": c2["images_per_s"], "flops_per_step": c2["flops_per_step"],
+                    "gpu_launches": c2["gpu_launches_per_step"] * args.steps}
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
     if args.config == 5:
         sweep = run_sweep(torch, samrs, lib, device, rank, sptr, stream, dist, world, args.steps, args.warmup)
         if rank == 0:
@@ -458,9 +479,11 @@ def run_ours(args):
         extra["3"] = run_config3(torch, samrs, lib, device, rank, sptr, stream, dist, world, min(K, 5), args.warmup)
         extra["5"] = run_sweep(torch, samrs, lib, device, rank, sptr, stream, dist, world, min(K, 5), args.warmup)
         extra["recompute_by_table_std"] = recompute_rates(torch, samrs, lib, device, sptr)
+        extra["2"] = run_config2(torch, samrs, device, rank, dist, world, min(K, 5), args.warmup, stream)
 
     neighbours = run_neighbours(samrs, lib, images, device, sptr, hbm, wl) \
         if not args.no_neighbours and args.config == 4 else None
+    gemms = run_gemms(samrs, lib, device, sptr, tf_burst) if not args.no_neighbours and args.config == 4 else None
 
     e2e = None
     if not args.no_e2e:
@@ -503,11 +526,134 @@ def run_ours(args):
             line["e2e"] = e2e
         if neighbours is not None:
             line["neighbours"] = neighbours
+        if gemms is not None:
+            line["gemms"] = gemms
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def config2_flops(images, c=768, heads=12, depth=12, global_layers=(2, 5, 8, 11)):
+    """Algorithmic FLOPs of one ViT-B stack step on the real tokens: the four projections (qkv 3C, proj C,
+    lin1 4C, lin2 4C: 2 * T * C * 12 C per block) and the attention (4 N^2 hd per head)."""
+    t, hd = images * 4096, c // heads
+    gemm = 2.0 * t * c * 12 * c * depth
+    att = sum(layer_flops(64, 64, images * heads, hd) if i in global_layers else
+              layer_flops(14, 14, images * WINDOWS * heads, hd) for i in range(depth))
+    return gemm, att
+
+
+def run_config2(torch, samrs, device, rank, dist, world, steps, warmup, stream):
+    """the ViT-B encoder block stack (12 blocks, global at 2, 5, 8, 11), f16, 8 images per
+    GPU, random-init weights ~ N(0, 0.02), tokens ~ N(0, 1), every op on this library's kernels (LayerNorm,
+    the fused qkv GEMM, the attention, the head merge, the proj / lin1 / lin2 GEMMs with their epilogues)."""
+    cfg = VIT_B_STACK
+    c, nh, images = cfg["c"], cfg["heads"], cfg["images"]
+    hd = c // nh
+    gen = torch.Generator(device=device).manual_seed(2000 + rank)
+
+    def rnd(*shape, std=0.02):
+        return (torch.randn(*shape, device=device, generator=gen) * std).half()
+
+    blocks = []
+    for i in range(cfg["depth"]):
+        win = 0 if i in cfg["global_layers"] else cfg["window"]
+        size = win if win else 64
+        p = dict(qkv_w=rnd(3 * c, c), qkv_b=rnd(3 * c), proj_w=rnd(c, c), proj_b=rnd(c), lin1_w=rnd(4 * c, c),
+                 lin1_b=rnd(4 * c), lin2_w=rnd(c, 4 * c), lin2_b=rnd(c), norm1_w=1 + rnd(c, std=0.1),
+                 norm1_b=rnd(c), norm2_w=1 + rnd(c, std=0.1), norm2_b=rnd(c), rel_pos_h=rnd(2 * size - 1, hd, std=0.5),
+                 rel_pos_w=rnd(2 * size - 1, hd, std=0.5))
+        blocks.append(samrs.Block(p, nh, win))
+    x0 = rnd(images, 64, 64, c, std=1.0)
+
+    def step():
+        y = x0
+        for blk in blocks:
+            y = blk.forward(y)
+        return y
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if samrs.device_status() != 0:
+        raise RuntimeError("device status word set during the config-2 warm-up")
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        y = step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b), dist, device)
+    gemm, att = config2_flops(images)
+    launches = sum(8 if i in cfg["global_layers"] else 9 for i in range(cfg["depth"]))
+    out = {"workload": "config 2: SAM ViT-B encoder block stack, f16, 12 blocks (global 2,5,8,11 / windowed 14x14), "
+                       "C 768, 12 heads, random-init weights N(0, 0.02)",
+           "images_per_gpu": images, "steps": steps, "ms_per_step": ms / steps,
+           "images_per_s": images * world * steps / (ms / 1e3),
+           "tflops": (gemm + att) * world * steps / (ms / 1e3) / 1e12,
+           "flops_per_step": {"gemm": gemm, "attention": att}, "gpu_launches_per_step": launches,
+           "checksum_rank0": float(y.float().sum().item()) if rank == 0 else None}
+    del blocks, x0, y
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_gemms(samrs, lib, device, sptr, tf_peak, images=32, reps=5):
+    """The tensor-core GEMMs with their fused epilogues at the ViT-H block's shapes (config 4, 32 images:
+    T = 131072 tokens, C = 1280), against torch (cuBLAS) plus the separate epilogue on the same inputs."""
+    import torch
+    import torch.nn.functional as F
+    t, c, nh, hd = images * 4096, 1280, 16, 80
+    g = torch.Generator(device=device).manual_seed(9)
+
+    def rnd(*shape, std=1.0):
+        return (torch.randn(*shape, device=device, generator=g) * std).to(torch.bfloat16)
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    out = {}
+    x = rnd(t, c)
+    res = rnd(t, c)
+    cases = {"qkv (window layout)": (3 * c, c), "proj + bias_residual": (c, c), "lin1 + bias_gelu": (4 * c, c),
+             "lin2 + bias_residual": (c, 4 * c)}
+    for name, (n, k) in cases.items():
+        a = x if k == c else rnd(t, k)
+        w, bias = rnd(n, k, std=0.02), rnd(n, std=0.02)
+        flops = 2.0 * t * n * k
+        if name.startswith("qkv"):
+            ours = lambda: samrs.qkv_linear_window(a, w, bias, images, 64, 64, 14, nh, hd)
+            ref = lambda: samrs.qkv_split_window(a @ w.T, bias, images, 64, 64, 14, nh, hd)
+            ref_name = "torch matmul (cuBLAS) + qkv_split_window kernel"
+        elif "gelu" in name:
+            ours = lambda: samrs.linear(a, w, bias, epilogue="bias_gelu")
+            ref = lambda: F.gelu(F.linear(a, w, bias))
+            ref_name = "torch F.linear (cuBLAS, bias in the epilogue) + F.gelu"
+        else:
+            ours = lambda: samrs.linear(a, w, bias, res=res, epilogue="bias_residual")
+            ref = lambda: torch.addmm(bias, a, w.T).add_(res)
+            ref_name = "torch addmm (cuBLAS) + add"
+        ms, ms_ref = timed(ours), timed(ref)
+        out[name] = {"shape": [t, n, k], "ms": ms, "tflops": flops / (ms / 1e3) / 1e12,
+                     "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / tf_peak, "torch_ms": ms_ref,
+                     "torch_tflops": flops / (ms_ref / 1e3) / 1e12, "torch_path": ref_name}
+    if samrs.device_status() != 0:
+        raise RuntimeError("device status word set by the GEMMs")
+    return out
 
 
 def run_config3(torch, samrs, lib, device, rank, sptr, stream, dist, world, steps, warmup):
@@ -744,7 +890,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[3, 4, 5], default=4)
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=4)
     ap.add_argument("--images", type=int, default=0, help="images per GPU (default: the config's, 32 for config 4)")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")

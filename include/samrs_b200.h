@@ -63,6 +63,11 @@ extern "C" {
 #define SAMRS_ERR_DEVICE (-4)      /* a kernel reported a fault in the device status word   */
 #define SAMRS_ERR_NODEVICE (-5)    /* no sm_100 device is current                           */
 
+/* epilogues of samrs_linear_fwd */
+#define SAMRS_EPI_BIAS 0          /* out = a.w^T + bias                       */
+#define SAMRS_EPI_BIAS_RESIDUAL 1 /* out = res + a.w^T + bias                 */
+#define SAMRS_EPI_BIAS_GELU 2     /* out = gelu_erf(a.w^T + bias)             */
+
 /* implementation selector for samrs_relpos_attn_fwd_ex */
 #define SAMRS_IMPL_AUTO 0  /* tensor-core kernels where the shape allows, SIMT kernel otherwise */
 #define SAMRS_IMPL_SIMT 1  /* CUDA-core fused flash kernel (any shape, any dtype)               */
@@ -122,6 +127,44 @@ SAMRS_API int samrs_qkv_split_window_fwd(const void* y, const void* bias, void* 
 SAMRS_API int samrs_window_merge_fwd(const void* attn, void* out, int64_t images, int h, int w, int ws, int nh, int hd,
                                      int dtype, void* stream);
 
+/*
+ * Linear layer with a fused epilogue on the tensor cores (tcgen05, f16 / bf16 I/O, f32 accumulation):
+ *   out[m, n] = epilogue( sum_k a[m, k] w[n, k] + bias[n] )
+ * w is the weight as stored in the checkpoint ([out, in]); the reference transposes it once into its
+ * `Linear` (src/cpu_gemm.rs:205-222, src/sam1/encoder.rs:61-63, 103-107) and multiplies with candle.
+ * Replaces, per epilogue:
+ *   SAMRS_EPI_BIAS           a Linear followed by a broadcast bias add
+ *   SAMRS_EPI_BIAS_RESIDUAL  src/kernels.rs:1040-1049 `bias_residual(res, Linear(x), bias)` (proj, mlp.lin2;
+ *                            CUDA kernel kernels/sam.cu:129-135), res [m, n]
+ *   SAMRS_EPI_BIAS_GELU      src/kernels.rs:1051-1061 `bias_gelu(Linear(x), bias)` (mlp.lin1; kernels/sam.cu:136-143,
+ *                            exact erf GELU)
+ * res is read only by SAMRS_EPI_BIAS_RESIDUAL (may be NULL otherwise; it may alias out).
+ * Limits: f16 / bf16, k % 8 == 0, n % 16 == 0, 16-byte aligned buffers, m < 2^31.
+ */
+SAMRS_API int samrs_linear_fwd(const void* a, const void* w, const void* bias, const void* res, void* out, int64_t m,
+                               int n, int k, int epilogue, int dtype, void* stream);
+
+/*
+ * The qkv projection of an attention block fused with the window partition and the head split:
+ *   x [images*h*w, C] (the block's normalised real tokens), w [3C, C], bias [3C], C = nh * hd ->
+ *   out = [q | kt | v] exactly as samrs_qkv_split_window_fwd lays it out (q, v: [bh, n, hd], kt: [bh, hd, n],
+ *   bh = window * nh + head, n = ws*ws, windows of the grid zero-padded to multiples of ws; ws = 0: one window
+ *   of h x w). The GEMM's epilogue adds the bias and stores each token's q / k / v straight into its window's
+ *   rows; a pad token gets the bias alone (its reference input is zero). Replaces src/sam1/encoder.rs:132-140
+ *   (window_partition) + :79 (qkv Linear) + src/kernels.rs:870-894 (`qkv_split`, kernels/sam.cu:108-128).
+ * Limits: f16 / bf16, hd % 16 == 0, 16-byte aligned buffers.
+ */
+SAMRS_API int samrs_qkv_linear_window_fwd(const void* x, const void* w, const void* bias, void* out, int64_t images,
+                                          int h, int w_grid, int ws, int nh, int hd, int dtype, void* stream);
+
+/*
+ * LayerNorm over the last dimension (the blocks' norm1 / norm2, candle_nn::LayerNorm with eps 1e-6,
+ * src/sam1/encoder.rs:100-102, 121, 127): out = (x - mean) / sqrt(var + eps) * weight + bias per row of c,
+ * statistics in f32. x, out: [rows, c]; weight, bias: [c].
+ */
+SAMRS_API int samrs_layer_norm_fwd(const void* x, const void* weight, const void* bias, void* out, int64_t rows,
+                                   int c, float eps, int dtype, void* stream);
+
 /* Message describing the last error returned on the calling thread ("" if none). */
 SAMRS_API const char* samrs_last_error(void);
 
@@ -141,6 +184,16 @@ SAMRS_API int samrs_abi_version(void);
  * No counterpart in the reference (its kernels cannot wait on anything).
  */
 SAMRS_API int samrs_device_status(void* stream, int clear);
+
+/*
+ * Test hooks of the failure path: every bounded wait of the kernels gives up after `wait_limit_cycles`
+ * SM clock cycles instead of ~1 s (0 restores the default), and CTA 0 of the global-layer kernel never
+ * loads key tile `withhold_key_tile` (-1: none). With both set, that CTA's wait for the tile runs out, the
+ * kernel records code 1 in the device status word and every CTA returns (nothing faults or hangs); a test
+ * then sees the status, clears it, restores the hooks and checks the next call. Synchronous. Test
+ * infrastructure with no counterpart in the reference.
+ */
+SAMRS_API int samrs_test_hooks(int64_t wait_limit_cycles, int withhold_key_tile);
 
 /*
  * Number of bf16 global-layer CTAs (one head x 256 query rows) that were recomputed by the exact second

@@ -148,3 +148,66 @@ def window_merge(attn, images, h, w, ws, nh, hd):
     else:
         grid = tok.reshape(images, h, w, nh * hd)
     return np.ascontiguousarray(grid.reshape(images * h * w, nh * hd))
+
+
+# ------------------------------------------------------------------------------------------------
+# The rest of the encoder block (src/sam1/encoder.rs:89-129), restated in numpy (f64 arithmetic on the
+# given values; the callers pass 16-bit-rounded inputs where the kernels see 16-bit inputs).
+# ------------------------------------------------------------------------------------------------
+
+def linear(a, w, bias=None):
+    """a [M, K] . w[N, K]^T (+ bias): the reference's Linear holds w transposed and multiplies
+    (src/cpu_gemm.rs:205-222, src/sam1/encoder.rs:61-63, 103-107)."""
+    y = np.asarray(a, np.float64) @ np.asarray(w, np.float64).T
+    return y if bias is None else y + np.asarray(bias, np.float64)
+
+
+def bias_residual(res, y, bias):
+    """res + y + bias[col] (src/kernels.rs:619-641)."""
+    return np.asarray(res, np.float64) + np.asarray(y, np.float64) + np.asarray(bias, np.float64)
+
+
+def bias_gelu(y, bias):
+    """gelu_erf(y + bias[col]) = 0.5 x (1 + erf(x / sqrt 2)) (src/kernels.rs:643-665)."""
+    from scipy.special import erf
+    x = np.asarray(y, np.float64) + np.asarray(bias, np.float64)
+    return 0.5 * x * (1.0 + erf(x / np.sqrt(2.0)))
+
+
+def layer_norm(x, weight, bias, eps=1e-6):
+    """LayerNorm over the last dim with the biased variance (candle_nn::LayerNorm, as the blocks' norm1 /
+    norm2 use it, src/sam1/encoder.rs:100-102)."""
+    x = np.asarray(x, np.float64)
+    mean = x.mean(-1, keepdims=True)
+    var = ((x - mean) ** 2).mean(-1, keepdims=True)
+    return (x - mean) / np.sqrt(var + eps) * np.asarray(weight, np.float64) + np.asarray(bias, np.float64)
+
+
+def attention_block(x, p, heads):
+    """Attention::forward (src/sam1/encoder.rs:73-85): x [nW, H, W, C] -> the output projection without its
+    bias [nW, H, W, C]; the attention itself is the exact-f32 oracle above."""
+    nw, h, w, c = x.shape
+    hd, n = c // heads, h * w
+    y = linear(x.reshape(nw * n, c), p["qkv_w"])
+    q, kt, v = qkv_split(y, p["qkv_b"], n, heads, hd)
+    rel = np.concatenate([p["rel_pos_h"], p["rel_pos_w"]], 0)
+    ctx = attention_relpos(q, kt, v, rel, h, w, hd ** -0.5)
+    out = ctx.reshape(nw, heads, n, hd).transpose(0, 2, 1, 3).reshape(nw * n, c)
+    return linear(out, p["proj_w"]).reshape(nw, h, w, c)
+
+
+def block_forward(x, p, heads, window, eps=1e-6):
+    """Block::forward (src/sam1/encoder.rs:115-129) in the reference's order: norm1, window_partition with
+    zero pad (windowed blocks), attention, window_unpartition crop, bias_residual, norm2, lin1 + bias_gelu,
+    lin2 + bias_residual. x [B, H, W, C] -> [B, H, W, C] (f64)."""
+    b, h, w, c = x.shape
+    y = layer_norm(x, p["norm1_w"], p["norm1_b"], eps)
+    if window:
+        parts = window_partition(y, window)
+        y = window_unpartition(attention_block(parts, p, heads), window, h, w)
+    else:
+        y = attention_block(y, p, heads)
+    x = bias_residual(x, y, p["proj_b"])
+    t = b * h * w
+    m = bias_gelu(linear(layer_norm(x, p["norm2_w"], p["norm2_b"], eps).reshape(t, c), p["lin1_w"]), p["lin1_b"])
+    return bias_residual(x, linear(m, p["lin2_w"]).reshape(b, h, w, c), p["lin2_b"])

@@ -9,6 +9,12 @@ reference; PyTorch CUDA tensors stand in for candle CUDA tensors (device memory 
     qkv_split(y, bias, n, nh, hd) -> (q, kt, v)          src/kernels.rs:870-894
     bmm(a, b)                                            src/kernels.rs:917-924
     Attention / window_partition / window_unpartition    src/sam1/encoder.rs:45-85, 132-145
+    linear(a, w, bias, res, epilogue)                    Linear + bias / bias_residual / bias_gelu
+                                                         (src/cpu_gemm.rs:205-222, src/kernels.rs:1040-1061)
+    qkv_linear_window(x, w, bias, ...)                   qkv Linear + window_partition + qkv_split, fused
+    layer_norm(x, weight, bias, eps)                     the blocks' norm1 / norm2 (src/sam1/encoder.rs:100-102)
+    Block                                                Block::forward (src/sam1/encoder.rs:89-129) on the
+                                                         library's kernels
 
 Every op runs a CUDA kernel of this package; a tensor that is not a contiguous CUDA tensor of
 f32/f16/bf16 raises, as the reference's `bail!` does (src/kernels.rs:1092,1097-1102). There is no
@@ -24,7 +30,7 @@ from ._abi import SamrsError
 
 __all__ = ["relpos_softmax", "attention_relpos", "attention_relpos_cpu", "qkv_split", "qkv_split_window",
            "window_merge", "bmm", "Attention", "window_partition", "window_unpartition", "device_status",
-           "recompute_count", "SamrsError"]
+           "recompute_count", "linear", "qkv_linear_window", "layer_norm", "Block", "SamrsError"]
 
 _DTYPES = {torch.float32: _abi.F32, torch.float16: _abi.F16, torch.bfloat16: _abi.BF16}
 _IMPLS = {"auto": _abi.IMPL_AUTO, "simt": _abi.IMPL_SIMT, "tc": _abi.IMPL_TC}
@@ -156,6 +162,63 @@ def window_merge(attn, images, h, w, ws, nh, hd):
     return out
 
 
+_EPIS = {"bias": _abi.EPI_BIAS, "bias_residual": _abi.EPI_BIAS_RESIDUAL, "bias_gelu": _abi.EPI_BIAS_GELU}
+
+
+def linear(a, w, bias, res=None, epilogue="bias", out=None):
+    """Tensor-core Linear with a fused epilogue: a [M, K] . w[N, K]^T + bias [N], then
+    "bias" (nothing more), "bias_residual" (+ res [M, N], src/kernels.rs:1040-1049) or "bias_gelu" (exact erf
+    GELU, src/kernels.rs:1051-1061). w is the weight as stored ([out, in]). f16 / bf16."""
+    if epilogue not in _EPIS:
+        raise SamrsError(_abi.ERR_INVALID, f"linear: unknown epilogue {epilogue!r}")
+    ts = (a, w, bias) if res is None else (a, w, bias, res)
+    code = _dtype_code(*ts)
+    if a.dim() != 2 or w.dim() != 2 or a.shape[1] != w.shape[1] or bias.numel() != w.shape[0]:
+        raise SamrsError(_abi.ERR_INVALID, f"linear: shapes a{tuple(a.shape)} w{tuple(w.shape)} bias{tuple(bias.shape)}")
+    m, k = a.shape
+    n = w.shape[0]
+    if epilogue == "bias_residual" and (res is None or tuple(res.shape) != (m, n)):
+        raise SamrsError(_abi.ERR_INVALID, "linear: bias_residual needs res [M, N]")
+    if out is None:
+        out = torch.empty(m, n, dtype=a.dtype, device=a.device)
+    _abi.check(_abi.lib().samrs_linear_fwd(a.data_ptr(), w.data_ptr(), bias.data_ptr(),
+                                           res.data_ptr() if res is not None else None, out.data_ptr(), m, n, k,
+                                           _EPIS[epilogue], code, _stream()))
+    return out
+
+
+def qkv_linear_window(x, w, bias, images, h, w_grid, ws, nh, hd):
+    """qkv Linear + window partition (zero pad) + bias + head split in one tensor-core GEMM: x [images*h*w, C]
+    (real tokens), w [3C, C], bias [3C] -> (q [BH,n,hd], kt [BH,hd,n], v [BH,n,hd]) as qkv_split_window returns
+    them (pad tokens get the bias)."""
+    code = _dtype_code(x, w, bias)
+    c = nh * hd
+    if x.dim() != 2 or tuple(x.shape) != (images * h * w_grid, c) or tuple(w.shape) != (3 * c, c) or \
+            bias.numel() != 3 * c:
+        raise SamrsError(_abi.ERR_INVALID, "qkv_linear_window: shape mismatch")
+    n, nwin = _win_counts(h, w_grid, ws)
+    bh = images * nwin * nh
+    packed = torch.empty(3 * bh * n * hd, dtype=x.dtype, device=x.device)
+    _abi.check(_abi.lib().samrs_qkv_linear_window_fwd(x.data_ptr(), w.data_ptr(), bias.data_ptr(), packed.data_ptr(),
+                                                      images, h, w_grid, ws, nh, hd, code, _stream()))
+    plane = bh * n * hd
+    return (packed[:plane].view(bh, n, hd), packed[plane:2 * plane].view(bh, hd, n),
+            packed[2 * plane:].view(bh, n, hd))
+
+
+def layer_norm(x, weight, bias, eps=1e-6, out=None):
+    """LayerNorm over the last dim (src/sam1/encoder.rs:100-102: candle_nn::LayerNorm, eps 1e-6)."""
+    code = _dtype_code(x, weight, bias)
+    c = x.shape[-1]
+    if weight.numel() != c or bias.numel() != c:
+        raise SamrsError(_abi.ERR_INVALID, "layer_norm: weight / bias size")
+    if out is None:
+        out = torch.empty_like(x)
+    _abi.check(_abi.lib().samrs_layer_norm_fwd(x.data_ptr(), weight.data_ptr(), bias.data_ptr(), out.data_ptr(),
+                                               x.numel() // c, c, float(eps), code, _stream()))
+    return out
+
+
 def bmm(a, b):
     """Batched [B,m,k] x [B,k,n] (src/kernels.rs:917-924); a plain library GEMM, as in the reference."""
     return torch.bmm(a, b)
@@ -228,3 +291,37 @@ class Attention:
 def vit_scale(hd):
     """scale = hd^-0.5 (src/sam1/encoder.rs:66)."""
     return 1.0 / math.sqrt(hd)
+
+
+class Block:
+    """SAM ViT encoder block, `Block::forward` of src/sam1/encoder.rs:89-129, on this library's kernels only:
+
+        y   = norm1(x)                                   layer_norm
+        q, kt, v = split(window_partition(y) Wqkv^T + b)  qkv_linear_window (pads get the bias)
+        a   = attention_relpos(q, kt, v, rel)            the fused tcgen05 attention
+        x   = x + merge(a) Wproj^T + bproj               window_merge, linear(bias_residual)
+        x   = x + gelu(norm2(x) W1^T + b1) W2^T + b2     layer_norm, linear(bias_gelu), linear(bias_residual)
+
+    The projections run on the real tokens only (a pad token's projection is the bias, and the crop drops
+    the pads' outputs), so the result is the reference's. Weights as stored ([out, in]); x [B, H, W, C]."""
+
+    def __init__(self, p, heads, window, eps=1e-6):
+        self.p, self.heads, self.window, self.eps = p, heads, window, eps
+        self.rel = torch.cat([p["rel_pos_h"], p["rel_pos_w"]], 0).contiguous()
+
+    def forward(self, x):
+        b, h, w, c = x.shape
+        nh, p = self.heads, self.p
+        hd = c // nh
+        t = b * h * w
+        xt = x.reshape(t, c)
+        y = layer_norm(xt, p["norm1_w"], p["norm1_b"], self.eps)
+        ws = self.window
+        q, kt, v = qkv_linear_window(y, p["qkv_w"], p["qkv_b"], b, h, w, ws, nh, hd)
+        wh, ww = (ws, ws) if ws else (h, w)
+        a = attention_relpos(q, kt, v, self.rel, wh, ww, float(hd) ** -0.5)
+        merged = window_merge(a, b, h, w, ws, nh, hd)
+        x1 = linear(merged, p["proj_w"], p["proj_b"], res=xt, epilogue="bias_residual")
+        y2 = layer_norm(x1, p["norm2_w"], p["norm2_b"], self.eps)
+        m = linear(y2, p["lin1_w"], p["lin1_b"], epilogue="bias_gelu")
+        return linear(m, p["lin2_w"], p["lin2_b"], res=x1, epilogue="bias_residual").reshape(b, h, w, c)

@@ -13,6 +13,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "samrs_b200.h")
 
 F32, F16, BF16 = 0, 1, 2
 IMPL_AUTO, IMPL_SIMT, IMPL_TC = 0, 1, 2
+EPI_BIAS, EPI_BIAS_RESIDUAL, EPI_BIAS_GELU = 0, 1, 2
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_LAUNCH, ERR_DEVICE, ERR_NODEVICE = 0, -1, -2, -3, -4, -5
 
 _lib = None
@@ -46,6 +47,10 @@ def lib():
         l.samrs_qkv_split_fwd.argtypes = [vp, vp, vp, i64, i32, i32, i32, i32, vp]
         l.samrs_qkv_split_window_fwd.argtypes = [vp, vp, vp, i64, i32, i32, i32, i32, i32, i32, vp]
         l.samrs_window_merge_fwd.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, i32, vp]
+        l.samrs_linear_fwd.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, vp]
+        l.samrs_qkv_linear_window_fwd.argtypes = [vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, i32, vp]
+        l.samrs_layer_norm_fwd.argtypes = [vp, vp, vp, vp, i64, i32, f32, i32, vp]
+        l.samrs_test_hooks.argtypes = [i64, i32]
         l.samrs_last_error.restype = ctypes.c_char_p
         l.samrs_device_status.argtypes = [vp, i32]
         l.samrs_recompute_count.argtypes = [vp, ctypes.POINTER(i64), i32]
@@ -53,7 +58,8 @@ def lib():
         for name in ("samrs_relpos_attn_fwd", "samrs_relpos_attn_fwd_ex", "samrs_relpos_softmax_fwd",
                      "samrs_qkv_split_fwd", "samrs_qkv_split_window_fwd", "samrs_window_merge_fwd",
                      "samrs_abi_version", "samrs_device_status", "samrs_recompute_count",
-                     "samrs_selftest_ex2"):
+                     "samrs_selftest_ex2", "samrs_linear_fwd", "samrs_qkv_linear_window_fwd",
+                     "samrs_layer_norm_fwd", "samrs_test_hooks"):
             getattr(l, name).restype = i32
         _lib = l
     return _lib

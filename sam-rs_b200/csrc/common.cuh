@@ -23,6 +23,12 @@ __device__ unsigned int g_status = 0;
 
 __device__ __forceinline__ void report(unsigned int code) { atomicCAS(&g_status, 0u, code); }
 
+// Test hooks (samrs_test_hooks): a shorter bound for every wait (cycles; 0 = the built-in ~1 s), and a key
+// tile whose K load CTA 0 of the global kernel never issues (-1 = none), so that a test can watch a bounded
+// wait run out, the kernel return with the status word set, and the library recover. Nothing else reads them.
+__device__ long long g_wait_limit = 0;
+__device__ int g_withhold_key_tile = -1;
+
 // Number of bf16 global-layer CTAs (one head x 256 query rows) that the exact fixup launch recomputed,
 // read and cleared by samrs_recompute_count(). A statistic for the caller, not read by any kernel.
 __device__ unsigned long long g_recomputed = 0;

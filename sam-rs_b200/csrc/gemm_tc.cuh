@@ -1,0 +1,291 @@
+// gemm_tc.cuh - tcgen05 (sm_100a) GEMM with fused epilogues for the projections around the attention:
+//   C[M, N] = A[M, K] . W[N, K]^T  (A: activations, W: a Linear weight as stored, [out, in]; both K-major)
+// followed, in the same kernel, by one of the epilogues of the reference's encoder block
+// (src/sam1/encoder.rs:73-85, 115-129):
+//   kEpiBias          out = C + bias                         (Linear + bias)
+//   kEpiBiasResidual  out = res + C + bias                   (proj / lin2 + `bias_residual`, kernels/sam.cu:129-135)
+//   kEpiBiasGelu      out = gelu_erf(C + bias)               (lin1 + `bias_gelu`, kernels/sam.cu:136-143)
+//   kEpiQkvWindow     q / kt / v = split(C + bias) written straight into the windowed attention layout
+//                     (the qkv projection + `qkv_split`, kernels/sam.cu:108-128, on the real tokens of a
+//                     window-partitioned grid, src/sam1/encoder.rs:132-140; the pad tokens are written by
+//                     qkv_pad_fill_kernel, see window_io.cuh)
+//
+// Structure: persistent grid (one CTA per SM) over 128 x 256 output tiles, rows of A fastest-varying tiles
+// sharing them back to back (the A tile stays in L2 across the N tiles of its row). 8 warps:
+//   warp 0   TMA producer: A [128 x 64] and W [256 x 64] boxes (128-byte swizzle) into a 4-stage ring
+//   warp 1   MMA issuer (the warp runs the loop, lane 0 issues): 4 x tcgen05.mma M=128 N=256 K=16 per stage
+//   warp 2   TMEM allocator (512 columns: two 256-column accumulators, so the epilogue of one tile overlaps
+//            the main loop of the next)
+//   warps 4-7 epilogue: thread = output row (TMEM lane), 16-column groups read with tcgen05.ld, the epilogue
+//            applied in f32, 16-byte stores of the row's columns.
+// No multicast anywhere; every wait is bounded (sm100::mbar_wait).
+#pragma once
+#include <cuda.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace samrs {
+namespace tgemm {
+
+constexpr int kThreads = 256;
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;  // 16 KB
+constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+enum Epi : int { kEpiBias = 0, kEpiBiasResidual = 1, kEpiBiasGelu = 2, kEpiQkvWindow = 3 };
+
+// Window geometry of the qkv epilogue: token m = (image, y, x) of an H x W grid cut into ws x ws windows
+// (ws = 0: the whole grid is one window), windows row-major per image over the grid padded up to multiples
+// of ws; q, kt, v planes back to back in `out`, bh = window * nh + head.
+struct QkvGeom {
+  int h, w, ws_h, ws_w, nwh, nww, nh, hd;
+  long plane;  // elements per q / kt / v plane
+};
+
+struct Params {
+  int M, N, K;
+  const void* bias;  // [N]
+  const void* res;   // [M, N] (kEpiBiasResidual)
+  void* out;         // [M, N], or the packed q | kt | v planes (kEpiQkvWindow)
+  QkvGeom g;
+};
+
+struct Bars {
+  uint64_t full[kStages], empty[kStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t final_mma;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <typename T>
+__device__ __forceinline__ void load16(const T* p, float (&f)[16]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+  const uint4 a = q[0], b = q[1];
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    } else {
+      const __half2 h2 = *reinterpret_cast<const __half2*>(&w[i]);
+      const float2 f2 = __half22float2(h2);
+      f[2 * i] = f2.x;
+      f[2 * i + 1] = f2.y;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store16(T* p, const float (&f)[16]) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = sm100::pack2(f[2 * i], f[2 * i + 1], kBf16);
+  uint4* q = reinterpret_cast<uint4*>(p);
+  q[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  q[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+// Exact (erf) GELU, as the reference's bias_gelu: 0.5 x (1 + erf(x / sqrt 2)).
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
+
+// The epilogue of 16 columns n0 .. n0 + 15 of row m (v: the f32 accumulators). The per-row window position
+// of the qkv epilogue (bh base and token index within the window) is computed once per tile row.
+template <typename T, int EPI>
+__device__ __forceinline__ void epilogue16(const Params& p, int m, int n0, float (&v)[16], long win_base, int n_in,
+                                           int npw) {
+  float b[16];
+  load16(static_cast<const T*>(p.bias) + n0, b);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] += b[j];
+  if constexpr (EPI == kEpiBias) {
+    store16(static_cast<T*>(p.out) + (long)m * p.N + n0, v);
+  } else if constexpr (EPI == kEpiBiasResidual) {
+    float r[16];
+    load16(static_cast<const T*>(p.res) + (long)m * p.N + n0, r);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] += r[j];
+    store16(static_cast<T*>(p.out) + (long)m * p.N + n0, v);
+  } else if constexpr (EPI == kEpiBiasGelu) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = gelu_erf(v[j]);
+    store16(static_cast<T*>(p.out) + (long)m * p.N + n0, v);
+  } else {
+    // column n0 -> (q / k / v, head, first dim); 16-column groups never straddle a head (hd % 16 == 0)
+    const int c = p.g.nh * p.g.hd;
+    const int which = n0 / c, cc = n0 - which * c;
+    const int head = cc / p.g.hd, d0 = cc - head * p.g.hd;
+    const long bh = win_base + head;
+    T* base = static_cast<T*>(p.out) + which * p.g.plane;
+    if (which == 1) {
+      // kt [bh][hd][n]: the 16 dims of this token are npw elements apart
+      T* dst = base + (bh * p.g.hd + d0) * (long)npw + n_in;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) dst[(long)j * npw] = from_f<T>(v[j]);
+    } else {
+      store16(base + (bh * npw + n_in) * (long)p.g.hd + d0, v);
+    }
+  }
+}
+
+template <typename T, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  using namespace sm100;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  if (__syncthreads_or(threadIdx.x == 0 && device_faulted())) return;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + kStages * kStageBytes);
+  volatile int* abort_flag = &bars->abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_blocks = (p.M + kBM - 1) / kBM, n_blocks = (p.N + kBN - 1) / kBN;
+  const int tiles = m_blocks * n_blocks;
+  const int nk = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&bars->final_mma, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int it = 0;
+      bool okk = true;
+      for (int tile = blockIdx.x; tile < tiles && okk; tile += gridDim.x) {
+        const int m0 = (tile / n_blocks) * kBM, n0 = (tile % n_blocks) * kBN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kStages;
+          if (it >= kStages && !mbar_wait(&bars->empty[s], ((it / kStages) - 1) & 1, abort_flag)) {
+            okk = false;
+            break;
+          }
+          uint8_t* st = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+          tma_load_2d(st, &tmA, &bars->full[s], kb * kBK, m0);
+          tma_load_2d(st + kABytes, &tmB, &bars->full[s], kb * kBK, n0);
+        }
+      }
+      if (*abort_flag) {
+        // drain this CTA's own copies still in flight before the CTA can exit
+        for (int j = it > kStages ? it - kStages : 0; j < it; ++j) mbar_drain(&bars->full[j % kStages], (j / kStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_f16(kBf16, kBM, kBN, false, false);
+    const uint32_t sb = smem_u32(smem);
+    // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart; K steps of 16 advance 32 B
+    const uint64_t dA = smem_desc(sb, 16, 1024, kLayoutSw128);
+    const uint64_t dB = smem_desc(sb + kABytes, 16, 1024, kLayoutSw128);
+    auto wait = [&](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag)); };
+    int it = 0, ti = 0;
+    bool okk = true;
+    for (int tile = blockIdx.x; tile < tiles && okk; tile += gridDim.x, ++ti) {
+      const int ab = ti & 1;
+      // the epilogue has read this accumulator's previous tile
+      if (ti >= 2 && !(okk = wait(&bars->acc_empty[ab], ((ti >> 1) - 1) & 1))) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem + ab * kBN;
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = it % kStages;
+        if (!(okk = wait(&bars->full[s], (it / kStages) & 1))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)
+          mma_ss_w(tacc, desc_add(dA, s * kStageBytes + 32 * k), desc_add(dB, s * kStageBytes + 32 * k), idesc,
+                   (kb > 0 || k > 0) ? 1u : 0u);
+        mma_commit_w(&bars->empty[s]);  // the stage may be refilled once these MMAs completed
+      }
+      if (!okk) break;
+      mma_commit_w(&bars->acc_full[ab]);
+    }
+    // every MMA issued by this warp has completed before the CTA tears down TMEM
+    mma_commit_w(&bars->final_mma);
+    mbar_drain(&bars->final_mma, 0);
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int wq = warp & 3;
+    int ti = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
+      const int ab = ti & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->acc_full[ab], (ti >> 1) & 1, abort_flag))) break;
+      tc_fence_after();
+      const int m0 = (tile / n_blocks) * kBM, n0 = (tile % n_blocks) * kBN;
+      const int m = m0 + 32 * wq + lane;
+      const bool row_ok = m < p.M;
+      long win_base = 0;
+      int n_in = 0, npw = 0;
+      if constexpr (EPI == kEpiQkvWindow) {
+        const QkvGeom& g = p.g;
+        const int hw = g.h * g.w;
+        const int img = m / hw, r = m - img * hw, y = r / g.w, x = r - y * g.w;
+        const int wy = y / g.ws_h, wx = x / g.ws_w;
+        win_base = ((long)img * g.nwh * g.nww + wy * g.nww + wx) * g.nh;
+        n_in = (y - wy * g.ws_h) * g.ws_w + (x - wx * g.ws_w);
+        npw = g.ws_h * g.ws_w;
+      }
+      const uint32_t tacc = tmem + ((uint32_t)(32 * wq) << 16) + ab * kBN;
+      uint32_t va[16], vb[16];
+      tmem_ld16(tacc, va);
+      static_for<0, kBN / 16>([&](auto gg) {
+        constexpr int grp = decltype(gg)::value;
+        uint32_t(&cur)[16] = (grp & 1) ? vb : va;
+        uint32_t(&nxt)[16] = (grp & 1) ? va : vb;
+        tmem_wait_ld_regs(cur);
+        if constexpr (grp + 1 < kBN / 16) {
+          tmem_ld16(tacc + 16 * (grp + 1), nxt);
+        } else {
+          // every column of this accumulator is in registers: hand it back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->acc_empty[ab]);
+        }
+        const int n = n0 + 16 * grp;
+        if (row_ok && n < p.N) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(cur[j]);
+          epilogue16<T, EPI>(p, m, n, v, win_base, n_in, npw);
+        }
+      });
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tgemm
+}  // namespace samrs

@@ -319,14 +319,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (Q and the tables went out with the barrier set-up) K and V of every key tile
       int issued_k = 0, issued_v = 0;
       if (lane == 0) {
+        // test hook: CTA 0 never loads this key tile (-1: none), so the MMA issuer's wait for it runs out
+        const int withhold = blockIdx.x == 0 ? *reinterpret_cast<volatile int*>(&g_withhold_key_tile) : -1;
         for (int j = 0; j < kNT; ++j) {
           const int jj = j, st = jj % kStages;
           const uint32_t prev = ((jj / kStages) - 1) & 1;
           if (jj >= kStages && !mbar_wait(&bars->k_empty[st], prev, abort_flag)) break;
-          mbar_arrive_expect_tx(&bars->k_full[st], L::kKBytes);
-          for (int a = 0; a < 2; ++a)
-            tma_load_2d(smem + L::OFF_K + st * L::kKBytes + a * L::kKAtom, &tmK, &bars->k_full[st],
-                        j * kBK + a * 64, (int)(bh * HD));
+          if (j != withhold) {
+            mbar_arrive_expect_tx(&bars->k_full[st], L::kKBytes);
+            for (int a = 0; a < 2; ++a)
+              tma_load_2d(smem + L::OFF_K + st * L::kKBytes + a * L::kKAtom, &tmK, &bars->k_full[st],
+                          j * kBK + a * 64, (int)(bh * HD));
+          }
           issued_k = jj + 1;
           if (jj >= kStages && !mbar_wait(&bars->v_empty[st], prev, abort_flag)) break;
           mbar_arrive_expect_tx(&bars->v_full[st], L::kVBytes);

@@ -13,6 +13,8 @@
 #include "../../include/samrs_b200.h"
 #include "common.cuh"
 #include "relpos_simt.cuh"
+#include "gemm_tc.cuh"
+#include "layernorm.cuh"
 #include "relpos_tc.cuh"
 #include "window_io.cuh"
 
@@ -211,6 +213,79 @@ int launch_merge(const void* attn, void* out, int64_t images, const WinGeom& g, 
   return launch_status("window_merge");
 }
 
+// ---------------------------------------------------------------------------------------- GEMM
+template <typename T, int EPI>
+int launch_gemm(const void* a, const void* w, const tgemm::Params& p, cudaStream_t st, int num_sms) {
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap ma, mb;
+  int rc = tcg::make_map(&ma, bf16, a, (uint64_t)p.K, (uint64_t)p.M, tgemm::kBK, tgemm::kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = tcg::make_map(&mb, bf16, w, (uint64_t)p.K, (uint64_t)p.N, tgemm::kBK, tgemm::kBN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return fail(SAMRS_ERR_LAUNCH, "linear: %s", tc_error_string(rc));
+  auto kern = tgemm::gemm_kernel<T, EPI>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tgemm::kSmemBytes) != cudaSuccess)
+    return fail(SAMRS_ERR_LAUNCH, "linear: cannot set the kernel's shared memory size");
+  const long tiles = (long)((p.M + tgemm::kBM - 1) / tgemm::kBM) * ((p.N + tgemm::kBN - 1) / tgemm::kBN);
+  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  kern<<<grid, tgemm::kThreads, tgemm::kSmemBytes, st>>>(ma, mb, p);
+  return launch_status("linear");
+}
+
+template <typename T>
+int launch_gemm_epi(int epi, const void* a, const void* w, const tgemm::Params& p, cudaStream_t st, int num_sms) {
+  switch (epi) {
+    case tgemm::kEpiBias:
+      return launch_gemm<T, tgemm::kEpiBias>(a, w, p, st, num_sms);
+    case tgemm::kEpiBiasResidual:
+      return launch_gemm<T, tgemm::kEpiBiasResidual>(a, w, p, st, num_sms);
+    case tgemm::kEpiBiasGelu:
+      return launch_gemm<T, tgemm::kEpiBiasGelu>(a, w, p, st, num_sms);
+    default:
+      return launch_gemm<T, tgemm::kEpiQkvWindow>(a, w, p, st, num_sms);
+  }
+}
+
+// Shape and pointer checks shared by the GEMM entry points (16-bit I/O, TMA-compatible strides).
+int check_gemm(const char* what, int64_t m, int n, int k, int dtype, const void* a, const void* w, const void* bias,
+               const void* out) {
+  if (dtype != SAMRS_F16 && dtype != SAMRS_BF16)
+    return fail(SAMRS_ERR_UNSUPPORTED, "%s: the tensor-core GEMM takes f16 or bf16 (dtype %d)", what, dtype);
+  if (m < 0 || m > 0x7fffffffLL || n < 1 || k < 1)
+    return fail(SAMRS_ERR_INVALID, "%s: bad shape m=%lld n=%d k=%d", what, (long long)m, n, k);
+  if (k % 8 != 0 || n % 16 != 0)
+    return fail(SAMRS_ERR_UNSUPPORTED, "%s: needs k %% 8 == 0 and n %% 16 == 0 (k=%d n=%d)", what, k, n);
+  if (m > 0 && (!a || !w || !bias || !out)) return fail(SAMRS_ERR_INVALID, "%s: null pointer", what);
+  if (m > 0 && !aligned16_all(a, w, bias)) return fail(SAMRS_ERR_INVALID, "%s: pointers must be 16-byte aligned", what);
+  if (m > 0 && !aligned16_all(out, out, out)) return fail(SAMRS_ERR_INVALID, "%s: pointers must be 16-byte aligned", what);
+  return SAMRS_OK;
+}
+
+// ---------------------------------------------------------------------------------------- LayerNorm
+template <typename T>
+int launch_layer_norm(const void* x, const void* wt, const void* b, void* out, int64_t rows, int c, float eps,
+                      cudaStream_t st, int num_sms) {
+  const long blocks = std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms * 16);
+  const auto* xp = static_cast<const T*>(x);
+  const auto* wp = static_cast<const T*>(wt);
+  const auto* bp = static_cast<const T*>(b);
+  auto* op = static_cast<T*>(out);
+  const bool vec = sizeof(T) == 2 && c % 8 == 0 && c <= 256 * kLnMaxChunks && aligned16_all(x, wt, b) &&
+                   aligned16_all(out, out, out);
+  if (vec) {
+    const int nch = (c + 255) / 256;
+    if (nch <= 3)
+      layer_norm_vec_kernel<T, 3><<<(unsigned)blocks, 256, 0, st>>>(xp, wp, bp, op, rows, c, eps);
+    else if (nch <= 4)
+      layer_norm_vec_kernel<T, 4><<<(unsigned)blocks, 256, 0, st>>>(xp, wp, bp, op, rows, c, eps);
+    else if (nch <= 5)
+      layer_norm_vec_kernel<T, 5><<<(unsigned)blocks, 256, 0, st>>>(xp, wp, bp, op, rows, c, eps);
+    else
+      layer_norm_vec_kernel<T, kLnMaxChunks><<<(unsigned)blocks, 256, 0, st>>>(xp, wp, bp, op, rows, c, eps);
+  } else {
+    layer_norm_any_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(xp, wp, bp, op, rows, c, eps);
+  }
+  return launch_status("layer_norm");
+}
+
 // Test hook of the windowed kernel's exp2 polynomial (sm100::ex2_poly2): y_poly = the polynomial, y_lib =
 // CUDA's exp2f, for the same x (pairs (2i, 2i+1), as the kernel evaluates them).
 __global__ void selftest_ex2_kernel(const float* __restrict__ x, float* __restrict__ y_poly, float* __restrict__ y_lib,
@@ -373,6 +448,108 @@ int samrs_window_merge_fwd(const void* attn, void* out, int64_t images, int h, i
     default:
       return launch_merge<__nv_bfloat16>(attn, out, images, g, dev->num_sms, st);
   }
+}
+
+int samrs_linear_fwd(const void* a, const void* w, const void* bias, const void* res, void* out, int64_t m, int n, int k,
+                     int epilogue, int dtype, void* stream) {
+  if (epilogue != SAMRS_EPI_BIAS && epilogue != SAMRS_EPI_BIAS_RESIDUAL && epilogue != SAMRS_EPI_BIAS_GELU)
+    return fail(SAMRS_ERR_INVALID, "linear: unknown epilogue %d", epilogue);
+  int rc = check_gemm("linear", m, n, k, dtype, a, w, bias, out);
+  if (rc) return rc;
+  if (epilogue == SAMRS_EPI_BIAS_RESIDUAL && m > 0 && (!res || !aligned16_all(res, res, res)))
+    return fail(SAMRS_ERR_INVALID, "linear: the residual must be a 16-byte aligned [m, n] buffer");
+  if (m == 0) return ok();
+  DevInfo* dev = nullptr;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  tgemm::Params p{};
+  p.M = (int)m;
+  p.N = n;
+  p.K = k;
+  p.bias = bias;
+  p.res = res;
+  p.out = out;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == SAMRS_BF16 ? launch_gemm_epi<__nv_bfloat16>(epilogue, a, w, p, st, dev->num_sms)
+                             : launch_gemm_epi<__half>(epilogue, a, w, p, st, dev->num_sms);
+}
+
+int samrs_qkv_linear_window_fwd(const void* x, const void* w, const void* bias, void* out, int64_t images, int h,
+                                int w_grid, int ws, int nh, int hd, int dtype, void* stream) {
+  WinGeom g;
+  int rc = win_geom("qkv_linear_window", images, h, w_grid, ws, nh, hd, &g);
+  if (rc) return rc;
+  if (hd % 16 != 0)
+    return fail(SAMRS_ERR_UNSUPPORTED, "qkv_linear_window: head_dim %d is not a multiple of 16", hd);
+  const int64_t m = images * (int64_t)h * w_grid;
+  const int c = nh * hd;
+  rc = check_gemm("qkv_linear_window", m, 3 * c, c, dtype, x, w, bias, out);
+  if (rc) return rc;
+  if (images == 0) return ok();
+  const int64_t bh = images * g.nwh * (int64_t)g.nww * nh;
+  if (bh * g.n() > 0x7fffffffLL || bh * g.n() * (int64_t)hd > ((int64_t)1 << 40))
+    return fail(SAMRS_ERR_UNSUPPORTED, "qkv_linear_window: batch too large");
+  DevInfo* dev = nullptr;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  tgemm::Params p{};
+  p.M = (int)m;
+  p.N = 3 * c;
+  p.K = c;
+  p.bias = bias;
+  p.out = out;
+  p.g = tgemm::QkvGeom{h, w_grid, g.wh, g.ww, g.nwh, g.nww, nh, hd, (long)(bh * g.n() * hd)};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = dtype == SAMRS_BF16 ? launch_gemm<__nv_bfloat16, tgemm::kEpiQkvWindow>(x, w, p, st, dev->num_sms)
+                           : launch_gemm<__half, tgemm::kEpiQkvWindow>(x, w, p, st, dev->num_sms);
+  if (rc) return rc;
+  // the pad tokens of the padded grid (none for ws = 0 or a grid that the windows tile exactly)
+  const int64_t pads = images * ((int64_t)g.nwh * g.wh * g.nww * g.ww - (int64_t)h * w_grid) * 3 * c;
+  if (pads > 0) {
+    const unsigned blocks = (unsigned)std::min<int64_t>((pads + 255) / 256, (int64_t)dev->num_sms * 8);
+    if (dtype == SAMRS_BF16)
+      qkv_pad_fill_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(bias),
+                                                                 static_cast<__nv_bfloat16*>(out), (long)images, g);
+    else
+      qkv_pad_fill_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(bias), static_cast<__half*>(out),
+                                                          (long)images, g);
+    return launch_status("qkv_pad_fill");
+  }
+  return ok();
+}
+
+int samrs_layer_norm_fwd(const void* x, const void* weight, const void* bias, void* out, int64_t rows, int c, float eps,
+                         int dtype, void* stream) {
+  if (dtype != SAMRS_F32 && dtype != SAMRS_F16 && dtype != SAMRS_BF16)
+    return fail(SAMRS_ERR_INVALID, "layer_norm: unsupported dtype code %d", dtype);
+  if (rows < 0 || c < 1) return fail(SAMRS_ERR_INVALID, "layer_norm: bad shape rows=%lld c=%d", (long long)rows, c);
+  if (!(eps >= 0.f)) return fail(SAMRS_ERR_INVALID, "layer_norm: eps must be >= 0");
+  if (rows == 0) return ok();
+  if (!x || !weight || !bias || !out) return fail(SAMRS_ERR_INVALID, "layer_norm: null pointer");
+  const size_t es = elem_size(dtype);
+  if (!aligned(x, es) || !aligned(weight, es) || !aligned(bias, es) || !aligned(out, es))
+    return fail(SAMRS_ERR_INVALID, "layer_norm: pointers must be aligned to the element size");
+  DevInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SAMRS_F32:
+      return launch_layer_norm<float>(x, weight, bias, out, rows, c, eps, st, dev->num_sms);
+    case SAMRS_F16:
+      return launch_layer_norm<__half>(x, weight, bias, out, rows, c, eps, st, dev->num_sms);
+    default:
+      return launch_layer_norm<__nv_bfloat16>(x, weight, bias, out, rows, c, eps, st, dev->num_sms);
+  }
+}
+
+int samrs_test_hooks(int64_t wait_limit_cycles, int withhold_key_tile) {
+  if (wait_limit_cycles < 0) return fail(SAMRS_ERR_INVALID, "test_hooks: negative wait limit");
+  const long long lim = (long long)wait_limit_cycles;
+  cudaError_t e = cudaMemcpyToSymbol(samrs::g_wait_limit, &lim, sizeof(lim));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(samrs::g_withhold_key_tile, &withhold_key_tile, sizeof(int));
+  if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "test_hooks: %s", cudaGetErrorString(e));
+  return ok();
 }
 
 int samrs_device_status(void* stream, int clear) {

@@ -52,11 +52,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The bound of a wait: kWaitCycles, or the test hook's shorter bound when one is set.
+__device__ __forceinline__ long long wait_limit() {
+  const long long l = *reinterpret_cast<volatile long long*>(&g_wait_limit);
+  return l > 0 ? l : kWaitCycles;
+}
+
 // Bounded wait for the phase with the given parity. Returns false if the bound is exceeded (recording
 // the timeout), or as soon as this CTA or any other CTA of the device has reported a fault.
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
+  const long long limit = wait_limit();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 0) {
@@ -64,7 +72,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         *abort_flag = 1;
         return false;
       }
-      if (clock64() - t0 > kWaitCycles) {
+      if (clock64() - t0 > limit) {
         report(kStatusWaitTimeout);
         *abort_flag = 1;
         return false;
@@ -76,8 +84,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Bounded wait used on the way out (draining): never reports, gives up after the bound.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const long long t0 = clock64();
+  const long long limit = wait_limit();
   while (!mbar_try_wait(bar, parity))
-    if (clock64() - t0 > kWaitCycles) return;
+    if (clock64() - t0 > limit) return;
 }
 
 // ---------------------------------------------------------------------------------- TMA

@@ -168,3 +168,42 @@ __global__ void __launch_bounds__(256) window_merge_kernel(const T* __restrict__
 }
 
 }  // namespace samrs
+
+namespace samrs {
+
+// Pad tokens of the window-partitioned grid: the reference zero-pads the normalised tokens before the qkv
+// projection (src/sam1/encoder.rs:132-140), so a pad token's q / k / v is the projection's bias alone.
+// Writes bias into q, kt and v at every (window, pad token, head) of the layout above. The pads of the
+// padded grid (nwh*wh x nww*ww) are its bottom strip (rows h.., every column) and then the right strip
+// (rows 0..h-1, columns w..); one thread per (pad token, column of 3C).
+template <typename T>
+__global__ void qkv_pad_fill_kernel(const T* __restrict__ bias, T* __restrict__ out, long images, WinGeom g) {
+  const int hp = g.nwh * g.wh, wp = g.nww * g.ww;
+  const long bottom = (long)(hp - g.h) * wp;
+  const long per_img = bottom + (long)g.h * (wp - g.w);
+  const int c = g.c(), c3 = 3 * c, n = g.n();
+  const long plane = images * g.nwh * g.nww * (long)g.nh * n * g.hd;
+  const long total = images * per_img * c3;
+  for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+    const int col = (int)(idx % c3);
+    const long pos = idx / c3;
+    const long img = pos / per_img, k = pos - img * per_img;
+    int y, x;
+    if (k < bottom) {
+      y = g.h + (int)(k / wp);
+      x = (int)(k % wp);
+    } else {
+      const long k2 = k - bottom;
+      y = (int)(k2 / (wp - g.w));
+      x = g.w + (int)(k2 % (wp - g.w));
+    }
+    const long win = (img * g.nwh + y / g.wh) * g.nww + x / g.ww;
+    const int n_in = (y % g.wh) * g.ww + x % g.ww;
+    const int which = col / c, cc = col - which * c, head = cc / g.hd, d = cc - head * g.hd;
+    const long bh = win * g.nh + head;
+    const long dst = which == 1 ? (bh * g.hd + d) * n + n_in : (bh * n + n_in) * g.hd + d;
+    out[which * plane + dst] = bias[col];
+  }
+}
+
+}  // namespace samrs

@@ -17,7 +17,8 @@ def test_library_exports_every_header_symbol():
     assert set(names) >= {"samrs_relpos_attn_fwd", "samrs_relpos_attn_fwd_ex", "samrs_relpos_softmax_fwd",
                           "samrs_qkv_split_fwd", "samrs_qkv_split_window_fwd", "samrs_window_merge_fwd",
                           "samrs_last_error", "samrs_abi_version", "samrs_device_status",
-                          "samrs_recompute_count", "samrs_selftest_ex2"}
+                          "samrs_recompute_count", "samrs_selftest_ex2", "samrs_linear_fwd",
+                          "samrs_qkv_linear_window_fwd", "samrs_layer_norm_fwd", "samrs_test_hooks"}
     lib = ctypes.CDLL(a.LIB_PATH)
     for n in names:
         assert hasattr(lib, n), n
@@ -98,3 +99,29 @@ def test_window_io_empty_and_null():
     assert a.lib().samrs_window_merge_fwd(0, 0, 0, 64, 64, 14, 16, 80, 2, None) == 0
     assert a.lib().samrs_qkv_split_window_fwd(0, 0, 0, 1, 64, 64, 14, 16, 80, 2, None) == -1
     assert a.lib().samrs_window_merge_fwd(0, 0, 1, 64, 64, 14, 16, 80, 2, None) == -1
+
+
+@pytest.mark.parametrize("args,code", [
+    (dict(dtype=0), -2),                  # f32: no tensor-core GEMM
+    (dict(k=100), -2), (dict(n=40), -2),  # k % 8, n % 16
+    (dict(m=-1), -1), (dict(n=0), -1),
+    (dict(epi=7), -1),
+])
+def test_linear_rejects_bad_arguments(args, code):
+    a = abi()
+    p = dict(m=4, n=32, k=64, epi=0, dtype=2)
+    p.update(args)
+    rc = a.lib().samrs_linear_fwd(0, 0, 0, 0, 0, p["m"], p["n"], p["k"], p["epi"], p["dtype"], None)
+    assert rc == code and a.lib().samrs_last_error()
+
+
+def test_linear_and_norm_empty_and_null():
+    a = abi()
+    assert a.lib().samrs_linear_fwd(0, 0, 0, 0, 0, 0, 32, 64, 1, 2, None) == 0
+    assert a.lib().samrs_linear_fwd(0, 0, 0, 0, 0, 4, 32, 64, 0, 2, None) == -1
+    assert a.lib().samrs_layer_norm_fwd(0, 0, 0, 0, 0, 768, 1e-6, 1, None) == 0
+    assert a.lib().samrs_layer_norm_fwd(0, 0, 0, 0, 3, 768, 1e-6, 1, None) == -1
+    assert a.lib().samrs_layer_norm_fwd(0, 0, 0, 0, 3, 768, -1.0, 1, None) == -1
+    assert a.lib().samrs_qkv_linear_window_fwd(0, 0, 0, 0, 0, 64, 64, 14, 12, 64, 1, None) == 0
+    assert a.lib().samrs_qkv_linear_window_fwd(0, 0, 0, 0, 1, 64, 64, 14, 12, 12, 1, None) == -2  # hd % 16
+    assert a.lib().samrs_qkv_linear_window_fwd(0, 0, 0, 0, 1, 64, 64, 14, 12, 64, 1, None) == -1  # null

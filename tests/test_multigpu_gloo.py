@@ -3,6 +3,7 @@ the device times reduce to the max over ranks, per-rank results gather in rank o
 computed on its own equals the same images taken from the single-process run."""
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -59,3 +60,48 @@ def test_two_rank_gather_and_max(tmp_path):
     batch = np.random.default_rng(5).standard_normal((6, 4)).astype(np.float64)
     assert out[7:].sum() == pytest.approx(batch.sum())
     assert out[7] == pytest.approx(batch[:3].sum()) and out[8] == pytest.approx(batch[3:].sum())
+
+
+def _failing_worker(rank, world, port, outdir, mode):
+    """Rank 1 fails on the host; rank 0 must see an error (not hang) within the process group's timeout."""
+    import datetime
+    import json
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if mode == "before_init" and rank == 1:
+        return  # never joins the rendezvous
+    t0 = time.time()
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    except Exception as e:  # rank 0 in "before_init": the store times out waiting for rank 1
+        if rank == 0:
+            json.dump({"error": type(e).__name__, "where": "init", "s": time.time() - t0},
+                      open(os.path.join(outdir, "r0.json"), "w"))
+        return
+    if mode == "after_init" and rank == 1:
+        os._exit(0)  # leaves between steps, with no collective in flight
+    try:
+        bench.gather_floats([1.0, 2.0], dist, torch.device("cpu"))
+        res = {"error": None}
+    except Exception as e:
+        res = {"error": type(e).__name__, "where": "gather", "s": time.time() - t0}
+    if rank == 0:
+        json.dump(res, open(os.path.join(outdir, "r0.json"), "w"))
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["before_init", "after_init"])
+def test_rank_failure_surfaces_as_an_error(tmp_path, mode):
+    """A rank that never joins, or exits after init, ends the other rank's next step with an error inside the
+    process group's timeout (the host side of the multi-GPU path; no GPU is involved)."""
+    import json
+    port = _free_port()
+    ctx = mp.start_processes(_failing_worker, args=(2, port, str(tmp_path), mode), nprocs=2, start_method="spawn",
+                             join=False)
+    deadline = time.time() + 60
+    while not ctx.join(timeout=1):
+        assert time.time() < deadline, "a rank hung"
+    r0 = json.load(open(tmp_path / "r0.json"))
+    assert r0["error"] is not None
+    assert r0["where"] == ("init" if mode == "before_init" else "gather")
+    assert r0["s"] < 30

@@ -110,3 +110,29 @@ def test_window_merge_inverts_split(images, h, w, ws, nh, hd):
         last = (nww - 1) * nh  # window (0, nww-1), head 0
         tok_pad = ws - 1  # column (nww-1)*ws + ws-1 >= w
         assert np.array_equal(q[last, tok_pad], b[:hd])
+
+
+def test_block_oracle_matches_torch_definitions():
+    """oracle.block_forward (numpy, the reference's order) against the same block written with torch's own
+    layer_norm / exact GELU / matmul on CPU, with the attention taken from the oracle in both."""
+    import torch
+    import torch.nn.functional as F
+    rng = np.random.default_rng(4)
+    c, nh, ws = 64, 2, 7
+    shapes = dict(qkv_w=(3 * c, c), qkv_b=(3 * c,), proj_w=(c, c), proj_b=(c,), lin1_w=(4 * c, c), lin1_b=(4 * c,),
+                  lin2_w=(c, 4 * c), lin2_b=(c,), norm1_w=(c,), norm1_b=(c,), norm2_w=(c,), norm2_b=(c,),
+                  rel_pos_h=(13, 32), rel_pos_w=(13, 32))
+    p = {k: (rng.standard_normal(s) * 0.1).astype(np.float64) for k, s in shapes.items()}
+    p["norm1_w"] += 1
+    p["norm2_w"] += 1
+    x = rng.standard_normal((1, 12, 12, c))
+    got = oracle.block_forward(x, p, nh, ws)
+    t = {k: torch.from_numpy(v) for k, v in p.items()}
+    xt = torch.from_numpy(x)
+    y = F.layer_norm(xt, (c,), t["norm1_w"], t["norm1_b"], 1e-6).numpy()
+    parts = oracle.window_partition(y, ws)
+    attn = oracle.window_unpartition(oracle.attention_block(parts, p, nh), ws, 12, 12)
+    x1 = xt + torch.from_numpy(np.asarray(attn)) + t["proj_b"]
+    hmid = F.gelu(F.layer_norm(x1, (c,), t["norm2_w"], t["norm2_b"], 1e-6) @ t["lin1_w"].T + t["lin1_b"])
+    want = (x1 + hmid @ t["lin2_w"].T + t["lin2_b"]).numpy()
+    assert np.abs(got - want).max() < 1e-9 * max(1.0, np.abs(want).max())
