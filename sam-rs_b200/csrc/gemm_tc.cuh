@@ -11,13 +11,15 @@
 //                     qkv_pad_fill_kernel, see window_io.cuh)
 //
 // Structure: persistent grid (one CTA per SM) over 128 x 256 output tiles, rows of A fastest-varying tiles
-// sharing them back to back (the A tile stays in L2 across the N tiles of its row). 8 warps:
+// sharing them back to back (the A tile stays in L2 across the N tiles of its row). 12 warps:
 //   warp 0   TMA producer: A [128 x 64] and W [256 x 64] boxes (128-byte swizzle) into a 4-stage ring
 //   warp 1   MMA issuer (the warp runs the loop, lane 0 issues): 4 x tcgen05.mma M=128 N=256 K=16 per stage
 //   warp 2   TMEM allocator (512 columns: two 256-column accumulators, so the epilogue of one tile overlaps
 //            the main loop of the next)
-//   warps 4-7 epilogue: thread = output row (TMEM lane), 16-column groups read with tcgen05.ld, the epilogue
-//            applied in f32, 16-byte stores of the row's columns.
+//   warps 4-11 epilogue: two warps per TMEM lane quarter, each taking half of the tile's columns; thread =
+//            output row (TMEM lane), 16-column groups read with tcgen05.ld, the epilogue applied in f32,
+//            16-byte stores of the row's columns. Two warps per quarter keep the epilogue (erf of the GELU,
+//            the k^T scatter of the qkv layout) shorter than the main loop of a tile.
 // No multicast anywhere; every wait is bounded (sm100::mbar_wait).
 #pragma once
 #include <cuda.h>
@@ -30,7 +32,8 @@
 namespace samrs {
 namespace tgemm {
 
-constexpr int kThreads = 256;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 128 + 32 * kEpiWarps;
 constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
@@ -46,10 +49,12 @@ enum Epi : int { kEpiBias = 0, kEpiBiasResidual = 1, kEpiBiasGelu = 2, kEpiQkvWi
 struct QkvGeom {
   int h, w, ws_h, ws_w, nwh, nww, nh, hd;
   long plane;  // elements per q / kt / v plane
+  int pairs;   // w even and the window width even (or one window): consecutive token pairs share a window row
 };
 
 struct Params {
   int M, N, K;
+  int group;  // M blocks whose tiles of one N block run side by side (1: the tiles of an M block run together)
   const void* bias;  // [N]
   const void* res;   // [M, N] (kEpiBiasResidual)
   void* out;         // [M, N], or the packed q | kt | v planes (kEpiQkvWindow)
@@ -100,8 +105,9 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + er
 // The epilogue of 16 columns n0 .. n0 + 15 of row m (v: the f32 accumulators). The per-row window position
 // of the qkv epilogue (bh base and token index within the window) is computed once per tile row.
 template <typename T, int EPI>
-__device__ __forceinline__ void epilogue16(const Params& p, int m, int n0, float (&v)[16], long win_base, int n_in,
-                                           int npw) {
+__device__ __forceinline__ void epilogue16(const Params& p, bool row_ok, int m, int n0, float (&v)[16], long win_base,
+                                           int n_in, int npw) {
+  if (EPI != kEpiQkvWindow && !row_ok) return;
   float b[16];
   load16(static_cast<const T*>(p.bias) + n0, b);
 #pragma unroll
@@ -125,8 +131,31 @@ __device__ __forceinline__ void epilogue16(const Params& p, int m, int n0, float
     const int head = cc / p.g.hd, d0 = cc - head * p.g.hd;
     const long bh = win_base + head;
     T* base = static_cast<T*>(p.out) + which * p.g.plane;
-    if (which == 1) {
-      // kt [bh][hd][n]: the 16 dims of this token are npw elements apart
+    if (which == 1 && p.g.pairs) {
+      // kt [bh][hd][n]: a token's 16 dims are npw elements apart. Lanes 2p and 2p+1 hold tokens x and x+1 of
+      // one grid row (x even; the rows of a lane pair are consecutive tokens), which share a window row when
+      // the window side is even, so they trade halves and each stores 8 dims of the token pair as 4-byte
+      // words: the even lane dims 0..7, the odd lane dims 8..15, both at the even lane's token.
+      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+      const int lane = threadIdx.x & 31;
+      const bool odd = lane & 1;
+      uint32_t own[8], oth[4];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) own[j] = sm100::pack2(v[2 * j], v[2 * j + 1], kBf16);  // dims 2j, 2j+1
+#pragma unroll
+      for (int j = 0; j < 4; ++j) oth[j] = __shfl_xor_sync(0xffffffffu, odd ? own[j] : own[4 + j], 1);
+      T* dst = base + (bh * p.g.hd + d0 + (odd ? 8 : 0)) * (long)npw + (n_in - (odd ? 1 : 0));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        // dim (odd ? 8 : 0) + j of the even token (lo) and the odd token (hi)
+        const uint32_t mine = odd ? own[4 + (j >> 1)] : own[j >> 1], theirs = oth[j >> 1];
+        const uint32_t ev = odd ? theirs : mine, od = odd ? mine : theirs;
+        const uint32_t w = (j & 1) ? ((ev >> 16) | (od & 0xFFFF0000u)) : ((ev & 0xFFFFu) | (od << 16));
+        if (row_ok) *reinterpret_cast<uint32_t*>(dst + (long)j * npw) = w;
+      }
+    } else if (!row_ok) {
+      return;
+    } else if (which == 1) {
       T* dst = base + (bh * p.g.hd + d0) * (long)npw + n_in;
 #pragma unroll
       for (int j = 0; j < 16; ++j) dst[(long)j * npw] = from_f<T>(v[j]);
@@ -134,6 +163,19 @@ __device__ __forceinline__ void epilogue16(const Params& p, int m, int n0, float
       store16(base + (bh * npw + n_in) * (long)p.g.hd + d0, v);
     }
   }
+}
+
+// Tile t -> (M block, N block). Groups of p.group M blocks: within a group the N block varies slowest, so
+// the group's M blocks of one N block are computed at the same time (the qkv epilogue's band of window rows:
+// each k^T row of a window is then written whole within one wave), and with p.group = 1 the N blocks of one
+// M block run back to back (its A tile stays in L2).
+__device__ __forceinline__ void tile_coords(const Params& p, int m_blocks, int n_blocks, int t, int& m0, int& n0) {
+  const int gsize = p.group * n_blocks;
+  const int grp = t / gsize, r = t - grp * gsize;
+  const int gm = m_blocks - grp * p.group < p.group ? m_blocks - grp * p.group : p.group;  // M blocks in the group
+  const int nb = r / gm, mb = grp * p.group + (r - nb * gm);
+  m0 = mb * kBM;
+  n0 = nb * kBN;
 }
 
 template <typename T, int EPI>
@@ -158,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&bars->acc_full[a], 1);
-      mbar_init(&bars->acc_empty[a], 4);  // one arrival per epilogue warp
+      mbar_init(&bars->acc_empty[a], kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(&bars->final_mma, 1);
     bars->abort_flag = 0;
@@ -181,7 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool okk = true;
       for (int tile = blockIdx.x; tile < tiles && okk; tile += gridDim.x) {
-        const int m0 = (tile / n_blocks) * kBM, n0 = (tile % n_blocks) * kBN;
+        int m0, n0;
+        tile_coords(p, m_blocks, n_blocks, tile, m0, n0);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % kStages;
           if (it >= kStages && !mbar_wait(&bars->empty[s], ((it / kStages) - 1) & 1, abort_flag)) {
@@ -233,13 +276,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_drain(&bars->final_mma, 0);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
-    const int wq = warp & 3;
+    const int wq = warp & 3;            // TMEM lane quarter
+    const int half = (warp - 4) >> 2;  // column half of the tile
+    constexpr int kGroups = kBN / 16 / (kEpiWarps / 4);
     int ti = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
       const int ab = ti & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->acc_full[ab], (ti >> 1) & 1, abort_flag))) break;
       tc_fence_after();
-      const int m0 = (tile / n_blocks) * kBM, n0 = (tile % n_blocks) * kBN;
+      int m0, n0;
+      tile_coords(p, m_blocks, n_blocks, tile, m0, n0);
       const int m = m0 + 32 * wq + lane;
       const bool row_ok = m < p.M;
       long win_base = 0;
@@ -253,15 +299,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         n_in = (y - wy * g.ws_h) * g.ws_w + (x - wx * g.ws_w);
         npw = g.ws_h * g.ws_w;
       }
-      const uint32_t tacc = tmem + ((uint32_t)(32 * wq) << 16) + ab * kBN;
+      const uint32_t tacc = tmem + ((uint32_t)(32 * wq) << 16) + ab * kBN + 16 * kGroups * half;
       uint32_t va[16], vb[16];
       tmem_ld16(tacc, va);
-      static_for<0, kBN / 16>([&](auto gg) {
+      static_for<0, kGroups>([&](auto gg) {
         constexpr int grp = decltype(gg)::value;
         uint32_t(&cur)[16] = (grp & 1) ? vb : va;
         uint32_t(&nxt)[16] = (grp & 1) ? va : vb;
         tmem_wait_ld_regs(cur);
-        if constexpr (grp + 1 < kBN / 16) {
+        if constexpr (grp + 1 < kGroups) {
           tmem_ld16(tacc + 16 * (grp + 1), nxt);
         } else {
           // every column of this accumulator is in registers: hand it back to the MMA warp
@@ -269,12 +315,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->acc_empty[ab]);
         }
-        const int n = n0 + 16 * grp;
-        if (row_ok && n < p.N) {
+        const int n = n0 + 16 * (kGroups * half + grp);
+        if (n < p.N) {  // warp-uniform (the qkv epilogue's lane pairs exchange values: every lane takes part)
           float v[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(cur[j]);
-          epilogue16<T, EPI>(p, m, n, v, win_base, n_in, npw);
+          epilogue16<T, EPI>(p, row_ok, m, n, v, win_base, n_in, npw);
         }
       });
     }

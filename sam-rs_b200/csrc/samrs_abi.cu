@@ -466,6 +466,7 @@ int samrs_linear_fwd(const void* a, const void* w, const void* bias, const void*
   p.M = (int)m;
   p.N = n;
   p.K = k;
+  p.group = 1;
   p.bias = bias;
   p.res = res;
   p.out = out;
@@ -496,22 +497,26 @@ int samrs_qkv_linear_window_fwd(const void* x, const void* w, const void* bias, 
   p.M = (int)m;
   p.N = 3 * c;
   p.K = c;
+  // the M blocks of one band of window rows (ws grid rows of every image column) run side by side
+  p.group = ws ? (int)std::max<int64_t>(1, std::min<int64_t>(16, ((int64_t)g.wh * w_grid + tgemm::kBM - 1) / tgemm::kBM)) : 1;
   p.bias = bias;
   p.out = out;
-  p.g = tgemm::QkvGeom{h, w_grid, g.wh, g.ww, g.nwh, g.nww, nh, hd, (long)(bh * g.n() * hd)};
+  const int pairs = w_grid % 2 == 0 && g.ww % 2 == 0;  // ws = 0: g.ww = w_grid
+  p.g = tgemm::QkvGeom{h, w_grid, g.wh, g.ww, g.nwh, g.nww, nh, hd, (long)(bh * g.n() * hd), pairs};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = dtype == SAMRS_BF16 ? launch_gemm<__nv_bfloat16, tgemm::kEpiQkvWindow>(x, w, p, st, dev->num_sms)
                            : launch_gemm<__half, tgemm::kEpiQkvWindow>(x, w, p, st, dev->num_sms);
   if (rc) return rc;
   // the pad tokens of the padded grid (none for ws = 0 or a grid that the windows tile exactly)
-  const int64_t pads = images * ((int64_t)g.nwh * g.wh * g.nww * g.ww - (int64_t)h * w_grid) * 3 * c;
+  const int64_t pads = images * ((int64_t)g.nwh * g.wh * g.nww * g.ww - (int64_t)h * w_grid);
   if (pads > 0) {
-    const unsigned blocks = (unsigned)std::min<int64_t>((pads + 255) / 256, (int64_t)dev->num_sms * 8);
+    const int64_t units = images * (g.nwh + g.nww) * (int64_t)nh;  // at least the edge windows x heads
+    const unsigned blocks = (unsigned)std::min<int64_t>(units, (int64_t)dev->num_sms * 16);
     if (dtype == SAMRS_BF16)
-      qkv_pad_fill_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(bias),
+      qkv_pad_fill_kernel<__nv_bfloat16><<<blocks, 128, 0, st>>>(static_cast<const __nv_bfloat16*>(bias),
                                                                  static_cast<__nv_bfloat16*>(out), (long)images, g);
     else
-      qkv_pad_fill_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(bias), static_cast<__half*>(out),
+      qkv_pad_fill_kernel<__half><<<blocks, 128, 0, st>>>(static_cast<const __half*>(bias), static_cast<__half*>(out),
                                                           (long)images, g);
     return launch_status("qkv_pad_fill");
   }

@@ -173,36 +173,45 @@ namespace samrs {
 
 // Pad tokens of the window-partitioned grid: the reference zero-pads the normalised tokens before the qkv
 // projection (src/sam1/encoder.rs:132-140), so a pad token's q / k / v is the projection's bias alone.
-// Writes bias into q, kt and v at every (window, pad token, head) of the layout above. The pads of the
-// padded grid (nwh*wh x nww*ww) are its bottom strip (rows h.., every column) and then the right strip
-// (rows 0..h-1, columns w..); one thread per (pad token, column of 3C).
+// Writes bias into q, kt and v at every (window, pad token, head) of the layout above. Only the windows of
+// the last window row / column hold pads; one CTA per (such window, head): q and v by 16-byte chunks of a
+// pad token's hd values (hd % 8 == 0), kt by one warp per dim row with the lanes over the row's tokens.
 template <typename T>
-__global__ void qkv_pad_fill_kernel(const T* __restrict__ bias, T* __restrict__ out, long images, WinGeom g) {
-  const int hp = g.nwh * g.wh, wp = g.nww * g.ww;
-  const long bottom = (long)(hp - g.h) * wp;
-  const long per_img = bottom + (long)g.h * (wp - g.w);
-  const int c = g.c(), c3 = 3 * c, n = g.n();
+__global__ void __launch_bounds__(128) qkv_pad_fill_kernel(const T* __restrict__ bias, T* __restrict__ out,
+                                                           long images, WinGeom g) {
+  const bool pad_rows = g.h % g.wh != 0, pad_cols = g.w % g.ww != 0;
+  // edge windows of an image: the last window row (if its rows pad), then the last window column (if its
+  // columns pad) without the corner already counted
+  const int n_bottom = pad_rows ? g.nww : 0;
+  const int n_edge = n_bottom + (pad_cols ? g.nwh - (pad_rows ? 1 : 0) : 0);
+  const int c = g.c(), n = g.n(), hd8 = g.hd / 8;
   const long plane = images * g.nwh * g.nww * (long)g.nh * n * g.hd;
-  const long total = images * per_img * c3;
-  for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
-    const int col = (int)(idx % c3);
-    const long pos = idx / c3;
-    const long img = pos / per_img, k = pos - img * per_img;
-    int y, x;
-    if (k < bottom) {
-      y = g.h + (int)(k / wp);
-      x = (int)(k % wp);
-    } else {
-      const long k2 = k - bottom;
-      y = (int)(k2 / (wp - g.w));
-      x = g.w + (int)(k2 % (wp - g.w));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (long unit = blockIdx.x; unit < images * n_edge * g.nh; unit += gridDim.x) {
+    const int head = (int)(unit % g.nh);
+    const long we = unit / g.nh;
+    const long img = we / n_edge;
+    const int e = (int)(we - img * n_edge);
+    const int wy = e < n_bottom ? g.nwh - 1 : e - n_bottom;
+    const int wx = e < n_bottom ? e : g.nww - 1;
+    const long bh = ((img * g.nwh + wy) * g.nww + wx) * g.nh + head;
+    const int y0 = wy * g.wh, x0 = wx * g.ww;
+    // q and v
+    for (int idx = threadIdx.x; idx < n * hd8; idx += blockDim.x) {
+      const int n_in = idx / hd8, ch = idx - n_in * hd8;
+      if (y0 + n_in / g.ww < g.h && x0 + n_in % g.ww < g.w) continue;
+      const int col = head * g.hd + 8 * ch;
+      const long off = (bh * n + n_in) * g.hd + 8 * ch;
+      *reinterpret_cast<uint4*>(out + off) = *reinterpret_cast<const uint4*>(bias + col);
+      *reinterpret_cast<uint4*>(out + 2 * plane + off) = *reinterpret_cast<const uint4*>(bias + 2 * c + col);
     }
-    const long win = (img * g.nwh + y / g.wh) * g.nww + x / g.ww;
-    const int n_in = (y % g.wh) * g.ww + x % g.ww;
-    const int which = col / c, cc = col - which * c, head = cc / g.hd, d = cc - head * g.hd;
-    const long bh = win * g.nh + head;
-    const long dst = which == 1 ? (bh * g.hd + d) * n + n_in : (bh * n + n_in) * g.hd + d;
-    out[which * plane + dst] = bias[col];
+    // kt
+    for (int d = warp; d < g.hd; d += nwarps) {
+      const T b = bias[c + head * g.hd + d];
+      T* row = out + plane + (bh * g.hd + d) * n;
+      for (int n_in = lane; n_in < n; n_in += 32)
+        if (y0 + n_in / g.ww >= g.h || x0 + n_in % g.ww >= g.w) row[n_in] = b;
+    }
   }
 }
 

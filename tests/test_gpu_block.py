@@ -42,7 +42,7 @@ def test_linear_epilogues(samrs, cuda, m, n, k, epi, dt):
 
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
 @pytest.mark.parametrize("images,h,w,ws,nh,hd", [(2, 64, 64, 14, 12, 64), (1, 64, 64, 0, 16, 80),
-                                                 (2, 13, 20, 7, 3, 32), (1, 14, 14, 14, 2, 16)])
+                                                 (2, 13, 20, 7, 3, 32), (1, 14, 14, 14, 2, 16), (3, 14, 10, 4, 2, 32)])
 def test_qkv_linear_window_bit_exact(samrs, cuda, images, h, w, ws, nh, hd, dt):
     """The fused qkv GEMM writes, element for element, what qkv_split_window makes of the same kernel's
     Linear output (round(a . w^T + b) in the I/O dtype): real tokens bit-exact, pad tokens = the bias."""
