@@ -753,10 +753,10 @@ def run_neighbours(samrs, lib, images, device, sptr, hbm, wl, reps=10):
     return out
 
 
-def copy_bandwidth(torch, device, dist, nbytes=1 << 30, reps=4):
+def copy_bandwidth(torch, device, dist, nbytes=1 << 30, reps=4, ratio=1):
     """Measured pinned host <-> device copy bandwidth of this rank (GB/s), with every rank copying at the same
     time (the host side is shared): one cudaMemcpyAsync per buffer, H2D and D2H each alone, then both at once
-    on two streams (the e2e leg overlaps them)."""
+    on two streams with `ratio` bytes up per byte down, as the e2e step moves them ("both": the aggregate)."""
     host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     host2 = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
@@ -770,16 +770,18 @@ def copy_bandwidth(torch, device, dist, nbytes=1 << 30, reps=4):
             dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        for _ in range(reps):
-            if name in ("h2d", "both"):
+        up = reps * (ratio if name == "both" else 1)
+        for i in range(max(up, reps)):
+            if name in ("h2d", "both") and i < up:
                 with torch.cuda.stream(s1):
                     dev.copy_(host, non_blocking=True)
-            if name in ("d2h", "both"):
+            if name in ("d2h", "both") and i < reps:
                 with torch.cuda.stream(s2):
                     host2.copy_(dev2, non_blocking=True)
         torch.cuda.synchronize()
         dt = time.perf_counter() - t0
-        res[name] = nbytes * reps * (2 if name == "both" else 1) / dt / 1e9
+        moved = {"h2d": reps, "d2h": reps, "both": up + reps}[name]
+        res[name] = nbytes * moved / dt / 1e9
     del host, host2, dev, dev2
     return res
 
@@ -868,7 +870,7 @@ def run_e2e(args, samrs, step, device, stream, dist, world, device_ms_per_step):
     ms = max_over_ranks(local_ms, dist, device)
     del host, dev
     torch.cuda.empty_cache()
-    bw = copy_bandwidth(torch, device, dist)
+    bw = copy_bandwidth(torch, device, dist, ratio=max(1, round(h2d / max(d2h, 1))))
     bw_min = {kname: max_over_ranks(-v, dist, device) * -1 for kname, v in bw.items()}  # slowest rank
     step_s = local_ms / k / 1e3
     # the host-link bound of one step: uploads and downloads overlap (full duplex), and neither beats the

@@ -205,7 +205,7 @@ SAMRS_API int samrs_recompute_count(void* stream, int64_t* count, int clear);
 
 /*
  * Self-test hook of the library's own exp2 polynomial (the FMA-pipe exponential the windowed kernel uses
- * for one key pair in four): y_poly[i] = the polynomial at x[i], y_lib[i] = CUDA's exp2f(x[i]); device
+ * for one key pair in eight): y_poly[i] = the polynomial at x[i], y_lib[i] = CUDA's exp2f(x[i]); device
  * f32 buffers of n elements. Test infrastructure; no counterpart in the reference.
  */
 SAMRS_API int samrs_selftest_ex2(const void* x, void* y_poly, void* y_lib, int64_t n, void* stream);

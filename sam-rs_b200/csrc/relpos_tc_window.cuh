@@ -143,7 +143,7 @@ __device__ __forceinline__ void chunk_max(const uint32_t (&sv)[32], float2 c2, c
 // (keys >= 196 get p = 0). The row sums come from the P.V MMA (ones block of V).
 template <int CH, int NE, bool BF16>
 __device__ __forceinline__ void chunk_exp(const uint32_t (&sv)[32], float2 c2, const Bias& b, uint32_t (&pk)[16]) {
-  // Staged: all exponents, then the exponentials (one pair in four on the FMA pipe), then packing.
+  // Staged: all exponents, then the exponentials (one pair in eight on the FMA pipe), then packing.
   constexpr int NV = (32 * CH + NE <= kN) ? NE : (kN - 32 * CH);  // keys of the chunk below kN (even)
   float x[32];
 #pragma unroll
@@ -156,7 +156,7 @@ __device__ __forceinline__ void chunk_exp(const uint32_t (&sv)[32], float2 c2, c
   }
 #pragma unroll
   for (int e = 0; e < NV; e += 2) {
-    if ((e & 6) == 6) {
+    if ((e & 14) == 14) {
       const float2 p = sm100::ex2_poly2(make_float2(x[e], x[e + 1]));
       x[e] = p.x;
       x[e + 1] = p.y;
