@@ -452,10 +452,14 @@ def run_ours(args):
         _, h, w, bh = next(g for g in step.geoms if g[0] == kind)
         avg_ms = statistics.mean(per_kind[kind])
         if kind == "global":
+            # the kernel runs inside a long step (tens of ms, steps back to back) under the 1000 W cap, so its
+            # denominator is the sustained bf16 figure; the burst fraction is reported beside it
             ach = layer_flops(h, w, bh, wl.hd) / (avg_ms / 1e3) / 1e12
-            peak = tf_burst
+            peak = tf_sust
             r = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                 "peak_source": f"{peak_src} bf16 burst (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback"}
+                 "peak_source": (f"{peak_src} bf16 sustained (MEASURED_PEAKS.json): timed inside a long step, "
+                                 "power-capped" if peak_src == "measured" else "fallback sustained"),
+                 "frac_of_burst": ach / tf_burst, "burst_peak": tf_burst}
         else:
             ach = layer_bytes(h, w, bh, wl.hd) / (avg_ms / 1e3) / 1e9
             peak = hbm
