@@ -81,6 +81,10 @@ extern "C" {
  * src/kernels.rs:131-225 `cpu::TiledAttention`). Limits: 1 <= h, w <= 128, 1 <= hd <= 128,
  * bh >= 0 (bh == 0 is a no-op). Pointers must be aligned to the element size; the tensor-core
  * path additionally wants 16-byte aligned q, v, out (it falls back to the SIMT kernel otherwise).
+ * bf16 64x64 layers run as two launches on `stream`: a single-pass kernel that marks an output block
+ * (one head x 256 rows) it cannot vouch for by a NaN in the block's first element, then an exact pass of
+ * the marked blocks; `out` is final only after both, i.e. in stream order (samrs_recompute_count tells
+ * how many blocks took the second pass).
  */
 SAMRS_API int samrs_relpos_attn_fwd(const void* q, const void* kt, const void* v, const void* table, void* out,
                           int64_t bh, int h, int w, int hd, float scale, int dtype, void* stream);
