@@ -11,15 +11,16 @@
 //                     qkv_pad_fill_kernel, see window_io.cuh)
 //
 // Structure: persistent grid (one CTA per SM) over 128 x 256 output tiles, rows of A fastest-varying tiles
-// sharing them back to back (the A tile stays in L2 across the N tiles of its row). 12 warps:
+// sharing them back to back (the A tile stays in L2 across the N tiles of its row). 12 or 20 warps:
 //   warp 0   TMA producer: A [128 x 64] and W [256 x 64] boxes (128-byte swizzle) into a 4-stage ring
 //   warp 1   MMA issuer (the warp runs the loop, lane 0 issues): 4 x tcgen05.mma M=128 N=256 K=16 per stage
 //   warp 2   TMEM allocator (512 columns: two 256-column accumulators, so the epilogue of one tile overlaps
 //            the main loop of the next)
-//   warps 4-11 epilogue: two warps per TMEM lane quarter, each taking half of the tile's columns; thread =
-//            output row (TMEM lane), 16-column groups read with tcgen05.ld, the epilogue applied in f32,
-//            16-byte stores of the row's columns. Two warps per quarter keep the epilogue (erf of the GELU,
-//            the k^T scatter of the qkv layout) shorter than the main loop of a tile.
+//   warps 4+ epilogue (epi_warps: 8, or 16 for the GELU): two or four warps per TMEM lane quarter, each
+//            taking a slice of the tile's columns; thread = output row (TMEM lane), 16-column groups read with
+//            tcgen05.ld, the epilogue applied in f32, 16-byte stores of the row's columns. Several warps per
+//            quarter keep the epilogue (erf of the GELU, the k^T scatter of the qkv layout) shorter than the
+//            main loop of a tile.
 // No multicast anywhere; every wait is bounded (sm100::mbar_wait).
 #pragma once
 #include <cuda.h>
@@ -32,8 +33,6 @@
 namespace samrs {
 namespace tgemm {
 
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 128 + 32 * kEpiWarps;
 constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
@@ -42,6 +41,12 @@ constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 enum Epi : int { kEpiBias = 0, kEpiBiasResidual = 1, kEpiBiasGelu = 2, kEpiQkvWindow = 3 };
+
+// Epilogue warps per CTA: 16 (four per TMEM lane quarter) for the erf GELU, whose per-tile epilogue at
+// K = 768 issues more instructions than the tile's main loop and needs the extra warps to hide latency;
+// 8 for the others, where more warps only add contention for the store path.
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == kEpiBiasGelu ? 16 : 8; }
+__host__ __device__ constexpr int threads_for(int epi) { return 128 + 32 * epi_warps(epi); }
 
 // Window geometry of the qkv epilogue: token m = (image, y, x) of an H x W grid cut into ws x ws windows
 // (ws = 0: the whole grid is one window), windows row-major per image over the grid padded up to multiples
@@ -179,9 +184,10 @@ __device__ __forceinline__ void tile_coords(const Params& p, int m_blocks, int n
 }
 
 template <typename T, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for(EPI), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
   using namespace sm100;
+  constexpr int kEpiWarps = epi_warps(EPI);
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   if (__syncthreads_or(threadIdx.x == 0 && device_faulted())) return;
@@ -277,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
     const int wq = warp & 3;            // TMEM lane quarter
-    const int half = (warp - 4) >> 2;  // column half of the tile
+    const int half = (warp - 4) >> 2;  // column slice of the tile (kEpiWarps / 4 slices)
     constexpr int kGroups = kBN / 16 / (kEpiWarps / 4);
     int ti = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {

@@ -226,7 +226,7 @@ int launch_gemm(const void* a, const void* w, const tgemm::Params& p, cudaStream
     return fail(SAMRS_ERR_LAUNCH, "linear: cannot set the kernel's shared memory size");
   const long tiles = (long)((p.M + tgemm::kBM - 1) / tgemm::kBM) * ((p.N + tgemm::kBN - 1) / tgemm::kBN);
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
-  kern<<<grid, tgemm::kThreads, tgemm::kSmemBytes, st>>>(ma, mb, p);
+  kern<<<grid, tgemm::threads_for(EPI), tgemm::kSmemBytes, st>>>(ma, mb, p);
   return launch_status("linear");
 }
 
