@@ -6,6 +6,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "relpos_tc_f32.cuh"
 #include "relpos_tc_global.cuh"
 #include "relpos_tc_window.cuh"
 #include "sm100.cuh"
@@ -132,6 +133,31 @@ int tc_launch_window(const void* q, const void* kt, const void* v, const void* t
   kern<<<grid, tcw::kThreads, smem, st>>>(mq, mv, static_cast<const T*>(table), static_cast<const T*>(kt),
                                          static_cast<T*>(out), (long)bh, scale);
   return 0;
+}
+
+// f32 I/O: the 3xTF32 kernel (relpos_tc_f32.cuh), one CTA per head and 128 query rows.
+template <int H, int W, int HD>
+int tc_launch_f32(const void* q, const void* kt, const void* v, const void* table, void* out, int64_t bh,
+                  float scale, cudaStream_t st) {
+  using G = tcf::Geo<H, W, HD>;
+  if (bh * G::kQTiles > 0x7fffffffLL) return 4;
+  auto kern = tcf::relpos_attn_f32<H, W, HD>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes) != cudaSuccess) return 5;
+  kern<<<(unsigned)(bh * G::kQTiles), tcf::kThreads, G::kSmemBytes, st>>>(
+      static_cast<const float*>(q), static_cast<const float*>(kt), static_cast<const float*>(v),
+      static_cast<const float*>(table), static_cast<float*>(out), scale);
+  return 0;
+}
+
+inline int tc_launch_f32(TcShape shape, const void* q, const void* kt, const void* v, const void* table, void* out,
+                         int64_t bh, int hd, float scale, cudaStream_t st) {
+  if (shape == TcShape::kGlobal)
+    return hd == 80 ? tc_launch_f32<64, 64, 80>(q, kt, v, table, out, bh, scale, st)
+                    : tc_launch_f32<64, 64, 64>(q, kt, v, table, out, bh, scale, st);
+  if (shape == TcShape::kWindow)
+    return hd == 80 ? tc_launch_f32<14, 14, 80>(q, kt, v, table, out, bh, scale, st)
+                    : tc_launch_f32<14, 14, 64>(q, kt, v, table, out, bh, scale, st);
+  return 1;
 }
 
 template <typename T>

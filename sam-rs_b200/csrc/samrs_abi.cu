@@ -328,12 +328,15 @@ int samrs_relpos_attn_fwd_ex(const void* q, const void* kt, const void* v, const
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-  if (impl != SAMRS_IMPL_SIMT && dtype != SAMRS_F32) {
+  if (impl != SAMRS_IMPL_SIMT) {
     const TcShape shape = tc_select(h, w, hd, q, kt, v, table, out);
     if (shape != TcShape::kNone) {
-      rc = dtype == SAMRS_BF16 ? tc_launch<__nv_bfloat16>(shape, q, kt, v, table, out, bh, h, w, hd, scale, st,
-                                                          dev->num_sms)
-                               : tc_launch<__half>(shape, q, kt, v, table, out, bh, h, w, hd, scale, st, dev->num_sms);
+      if (dtype == SAMRS_F32)
+        rc = tc_launch_f32(shape, q, kt, v, table, out, bh, hd, scale, st);
+      else
+        rc = dtype == SAMRS_BF16
+                 ? tc_launch<__nv_bfloat16>(shape, q, kt, v, table, out, bh, h, w, hd, scale, st, dev->num_sms)
+                 : tc_launch<__half>(shape, q, kt, v, table, out, bh, h, w, hd, scale, st, dev->num_sms);
       if (rc == 0) return launch_status("relpos_attn_tc");
       return fail(SAMRS_ERR_LAUNCH, "relpos_attn_tc: %s", tc_error_string(rc));
     }

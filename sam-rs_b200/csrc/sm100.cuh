@@ -204,6 +204,19 @@ __device__ __forceinline__ void mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint6
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem], kind::tf32 (32-bit operands of which the MMA uses the TF32 part, f32
+// accumulate). A is K-major in TMEM, one 32-bit value per column; K = 8 per instruction.
+__device__ __forceinline__ void mma_ts_tf32_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_commit_w(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
@@ -356,6 +369,13 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a
          | ((bf16 ? 1u : 0u) << 7)                  // A format
          | ((bf16 ? 1u : 0u) << 10)                 // B format
          | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor of kind::tf32 with f32 accumulation (A/B format 2). A is K-major (from TMEM);
+// b_mn: B is MN-major in shared memory.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
 }
 

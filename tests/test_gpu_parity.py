@@ -123,7 +123,7 @@ def test_full_batch_properties(samrs, cuda, h, w, bh, hd):
     assert err < HALF_TOL, err
 
 
-@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("hd", [64, 80])
 def test_global_late_max_jumps(samrs, cuda, hd, dt):
     """Row maxima that jump late in the key sequence (64x64 global layer): the online softmax's rescaling.
@@ -149,7 +149,33 @@ def test_global_late_max_jumps(samrs, cuda, hd, dt):
     assert samrs.device_status() == 0
     ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, w, scale)
     err = parity_err(out.float().cpu().numpy(), ref, dt)
-    assert err < HALF_TOL, err
+    assert err < tol(dt), err
+
+
+@pytest.mark.parametrize("h,w,bh,hd", [(64, 64, 3, 80), (14, 14, 37, 80), (14, 14, 50, 64), (64, 64, 4, 64)])
+def test_f32_tensor_core_path(samrs, cuda, h, w, bh, hd):
+    """f32 I/O on the tensor cores (kind::tf32 MMAs on operands split in two TF32 terms), forced with
+    impl="tc", against the oracle at the f32 bar: ViT-B/L (hd 64) and ViT-H (hd 80) global and windowed shapes."""
+    err = run_case(samrs, cuda, h, w, bh, hd, "f32", "tc", seed=bh * 5 + hd, table_std=0.5)
+    assert err < F32_TOL, err
+
+
+@pytest.mark.parametrize("hd", [64, 80])
+def test_window_f32_late_max(samrs, cuda, hd):
+    """f32 windowed layers: row maxima that jump by 40-100 log2 units in the second, third or last (partly
+    masked) 64-key tile, so that the lazily rescaled running maximum must rescale O."""
+    h = w = 14
+    q, kt, v, t = make_inputs(h, w, 12, hd, seed=hd + 3, table_std=0.5)
+    q[:, :, 0] = 4.0
+    for b in range(12):
+        kt[b, 0, [70, 140, 195][b % 3]] = 40.0 + 20.0 * (b % 4)
+    scale = hd ** -0.5
+    qd, ktd, vd, td = (to_dev(x, "f32", cuda) for x in (q, kt, v, t))
+    out = samrs.attention_relpos(qd, ktd, vd, td, h, w, scale, impl="tc")
+    assert samrs.device_status() == 0
+    ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, w, scale)
+    err = parity_err(out.float().cpu().numpy(), ref, "f32")
+    assert err < F32_TOL, err
 
 
 @pytest.mark.parametrize("table_std", [0.1, 0.5, 8.0])
