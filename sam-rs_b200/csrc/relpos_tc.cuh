@@ -142,6 +142,8 @@ int tc_launch_f32(const void* q, const void* kt, const void* v, const void* tabl
   using G = tcf::Geo<H, W, HD>;
   if (bh * G::kQTiles > 0x7fffffffLL) return 4;
   auto kern = tcf::relpos_attn_f32<H, W, HD>;
+  static const bool regs_ok = regs_cover_split(kern, tcf::kThreads, 128 * tcf::kRegsLow + 384 * tcf::kRegsHigh);
+  if (!regs_ok) return 6;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes) != cudaSuccess) return 5;
   kern<<<(unsigned)(bh * G::kQTiles), tcf::kThreads, G::kSmemBytes, st>>>(
       static_cast<const float*>(q), static_cast<const float*>(kt), static_cast<const float*>(v),

@@ -116,6 +116,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 // 8-byte global -> shared copy (both addresses 8-byte aligned), completion via cp_async_wait_all.
 // Bulk (non-tensor) store shared -> global, tracked by this thread's bulk groups. Both addresses 16-byte
 // aligned, size a multiple of 16.
+// Bulk (non-tensor) load global -> shared of this CTA, completion counted on `bar` (bytes). Both addresses
+// 16-byte aligned, size a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_load(void* sdst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(sdst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
                "r"(bytes)
