@@ -12,7 +12,9 @@ layers in encoder order (src/sam1/encoder.rs:19-23), bf16:
     config 5: config 4 swept over 8, 16, 32, 64 and 128 images per GPU
     config 2: the whole ViT-B encoder block stack (LayerNorm, the qkv / proj / MLP GEMMs with their fused
         epilogues, the attention), f16, 8 images per GPU, 12 blocks
-The default run prints the config-4 line and carries configs 2, 3 and 5 (shorter timings) in its "configs"
+    config 1: the ViT-B op in f32, one image: the windowed and the global layer, each through the f32
+        tensor-core kernel (3xTF32) and through the CUDA-core kernel
+The default run prints the config-4 line and carries configs 1, 2, 3 and 5 (shorter timings) in its "configs"
 object, and the block's GEMMs at the ViT-H shapes in "gemms"; --config 2 / 3 / 5 print their own line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
@@ -484,6 +486,7 @@ def run_ours(args):
         extra["5"] = run_sweep(torch, samrs, lib, device, rank, sptr, stream, dist, world, min(K, 5), args.warmup)
         extra["recompute_by_table_std"] = recompute_rates(torch, samrs, lib, device, sptr)
         extra["2"] = run_config2(torch, samrs, device, rank, dist, world, min(K, 5), args.warmup, stream)
+        extra["1"] = run_config1(torch, samrs, device)
 
     neighbours = run_neighbours(samrs, lib, images, device, sptr, hbm, wl) \
         if not args.no_neighbours and args.config == 4 else None
@@ -674,6 +677,52 @@ def run_config3(torch, samrs, lib, device, rank, sptr, stream, dist, world, step
         out[f"{kind}_gbs"] = layer_bytes(h, w, bh, 64) / (ms / 1e3) / 1e9
     out["checksums_rank0"] = step.checksums() if rank == 0 else None
     del step
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_config1(torch, samrs, device, reps=20, warmup=3):
+    """BASELINE config 1: the ViT-B op in f32, one image (windowed: 25 windows x 12 heads of 14x14, hd 64;
+    global: 12 heads of 64x64, hd 64; tables N(0, 0.5)). Each layer through the f32 tensor-core kernel (3xTF32
+    tcgen05, the library's default for f32) and through the CUDA-core kernel, L2 flushed before every timed
+    launch (the inputs fit in L2). Also the f32 kernel at the config-4 layer shapes (32 ViT-H images)."""
+    g = torch.Generator(device=device).manual_seed(101)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        total = 0.0
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            total += a.elapsed_time(b)
+        return total / reps
+
+    out = {"workload": "config 1: ViT-B attention op, f32, 1 image (windowed 300 heads 14x14 + global 12 heads 64x64, "
+                       "hd 64); L2 flushed before each timed launch"}
+    for kind, h, bh, hd, impls in (("window", 14, 300, 64, ("tc", "simt")), ("global", 64, 12, 64, ("tc", "simt")),
+                                   ("window_vith32", 14, 12800, 80, ("tc",)), ("global_vith32", 64, 512, 80, ("tc",))):
+        n = h * h
+        q = torch.randn(bh, n, hd, device=device, generator=g)
+        kt = torch.randn(bh, hd, n, device=device, generator=g)
+        v = torch.randn(bh, n, hd, device=device, generator=g)
+        t = torch.randn(4 * h - 2, hd, device=device, generator=g) * 0.5
+        o = torch.empty_like(q)
+        for impl in impls:
+            ms = timed(lambda: samrs.attention_relpos(q, kt, v, t, h, h, hd ** -0.5, impl=impl, out=o))
+            out[f"{kind}_{impl}_ms"] = ms
+            out[f"{kind}_{impl}_tflops"] = layer_flops(h, h, bh, hd) / (ms / 1e3) / 1e12
+        del q, kt, v, o
+    if samrs.device_status() != 0:
+        raise RuntimeError("device status word set by the f32 layers")
+    out["layer_ms_tc"] = out["window_tc_ms"] + out["global_tc_ms"]
+    out["layer_ms_simt"] = out["window_simt_ms"] + out["global_simt_ms"]
+    del flush
     torch.cuda.empty_cache()
     return out
 

@@ -79,8 +79,10 @@ extern "C" {
  *   with r = i*w + j, k = kh*w + kw, Th = table[0 : 2h-1], Tw = table[2h-1 : 2h-1+2w-1].
  * Replaces src/kernels.rs:896-906 (`attention_relpos_cpu`, whose f32 CPU body is
  * src/kernels.rs:131-225 `cpu::TiledAttention`). Limits: 1 <= h, w <= 128, 1 <= hd <= 128,
- * bh >= 0 (bh == 0 is a no-op). Pointers must be aligned to the element size; the tensor-core
- * path additionally wants 16-byte aligned q, v, out (it falls back to the SIMT kernel otherwise).
+ * bh >= 0 (bh == 0 is a no-op). Pointers must be aligned to the element size. 64x64 and 14x14 layers
+ * with hd 64 or 80 run on the tensor cores in every dtype (f32 as three TF32 products per contraction,
+ * about 2^-20 relative error per product) when q, kt, v, table and out are 16-byte aligned; other shapes
+ * run on the SIMT kernel.
  * bf16 64x64 layers run as two launches on `stream`: a single-pass kernel that marks an output block
  * (one head x 256 rows) it cannot vouch for by a NaN in the block's first element, then an exact pass of
  * the marked blocks; `out` is final only after both, i.e. in stream order (samrs_recompute_count tells
