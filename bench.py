@@ -15,9 +15,10 @@ layers in encoder order (src/sam1/encoder.rs:19-23), bf16:
     config 1: the ViT-B op in f32, one image: the windowed and the global layer, each through the f32
         tensor-core kernel (3xTF32) and through the CUDA-core kernel
 The default run prints the config-4 line and carries configs 1, 2, 3 and 5 (shorter timings) in its "configs"
-object, and the block's GEMMs at the ViT-H shapes in "gemms"; --config 2 / 3 / 5 print their own line.
+object, and the block's GEMMs at the ViT-H shapes in "gemms"; --config 1 / 2 / 3 / 5 print their own line
+(--config 1: one step = the windowed and the global f32 layer of one image, K steps per layer kind).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4|5]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N   (one rank per GPU)
 
 Multi-GPU: the image batch is sharded (the per-GPU image count is fixed, weak scaling); there is no collective
@@ -399,6 +400,23 @@ def run_ours(args):
     stream = torch.cuda.current_stream(device)
     sptr = stream.cuda_stream
     hbm, tf_burst, tf_sust, peak_src = load_peaks()
+
+    if args.config == 1:
+        c1 = run_config1(torch, samrs, device, reps=args.steps, warmup=args.warmup)
+        if rank == 0:
+            ms = c1["layer_ms_tc"]
+            flops = layer_flops(14, 14, 300, 64) + layer_flops(64, 64, 12, 64)
+            line = {"metric": METRIC, "value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": world,
+                    "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                    "data": "synthetic (seeded N(0,1) activations, N(0,0.5) rel-pos tables)",
+                    "config": {"workload": c1["workload"], "parallelism": f"dp{world}"},
+                    "layers": c1, "gpu_launches": 6 * args.steps}
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
 
     if args.config == 2:
         c2 = run_config2(torch, samrs, device, rank, dist, world, args.steps, args.warmup, stream)
@@ -945,7 +963,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=4)
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5], default=4)
     ap.add_argument("--images", type=int, default=0, help="images per GPU (default: the config's, 32 for config 4)")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
