@@ -109,9 +109,25 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + er
 
 // The epilogue of 16 columns n0 .. n0 + 15 of row m (v: the f32 accumulators). The per-row window position
 // of the qkv epilogue (bh base and token index within the window) is computed once per tile row.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4 (&q)[2], float (&f)[16]) {
+  const uint32_t w[8] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    } else {
+      const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      f[2 * i] = f2.x;
+      f[2 * i + 1] = f2.y;
+    }
+  }
+}
+
 template <typename T, int EPI>
 __device__ __forceinline__ void epilogue16(const Params& p, bool row_ok, int m, int n0, float (&v)[16], long win_base,
-                                           int n_in, int npw) {
+                                           int n_in, int npw, const uint4 (&res)[2]) {
   if (EPI != kEpiQkvWindow && !row_ok) return;
   float b[16];
   load16(static_cast<const T*>(p.bias) + n0, b);
@@ -121,7 +137,7 @@ __device__ __forceinline__ void epilogue16(const Params& p, bool row_ok, int m, 
     store16(static_cast<T*>(p.out) + (long)m * p.N + n0, v);
   } else if constexpr (EPI == kEpiBiasResidual) {
     float r[16];
-    load16(static_cast<const T*>(p.res) + (long)m * p.N + n0, r);
+    unpack16<T>(res, r);  // loaded before the tile's accumulator was ready
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] += r[j];
     store16(static_cast<T*>(p.out) + (long)m * p.N + n0, v);
@@ -288,12 +304,28 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     int ti = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
       const int ab = ti & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->acc_full[ab], (ti >> 1) & 1, abort_flag))) break;
-      tc_fence_after();
       int m0, n0;
       tile_coords(p, m_blocks, n_blocks, tile, m0, n0);
       const int m = m0 + 32 * wq + lane;
       const bool row_ok = m < p.M;
+      // the residual's columns of this thread, loaded while the tile's main loop still runs
+      constexpr int kRes = EPI == kEpiBiasResidual ? kGroups : 1;
+      uint4 res[kRes][2];
+      if constexpr (EPI == kEpiBiasResidual) {
+#pragma unroll
+        for (int grp = 0; grp < kGroups; ++grp) {
+          const int n = n0 + 16 * (kGroups * half + grp);
+          if (row_ok && n < p.N) {
+            const uint4* q = reinterpret_cast<const uint4*>(static_cast<const T*>(p.res) + (long)m * p.N + n);
+            res[grp][0] = q[0];
+            res[grp][1] = q[1];
+          } else {
+            res[grp][0] = res[grp][1] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->acc_full[ab], (ti >> 1) & 1, abort_flag))) break;
+      tc_fence_after();
       long win_base = 0;
       int n_in = 0, npw = 0;
       if constexpr (EPI == kEpiQkvWindow) {
@@ -326,7 +358,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
           float v[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(cur[j]);
-          epilogue16<T, EPI>(p, row_ok, m, n, v, win_base, n_in, npw);
+          epilogue16<T, EPI>(p, row_ok, m, n, v, win_base, n_in, npw, res[EPI == kEpiBiasResidual ? grp : 0]);
         }
       });
     }
