@@ -118,6 +118,27 @@ __device__ __forceinline__ float dot_row(const float (&q)[HD], const float* t) {
   return (a[0] + a[1]) + (a[2] + a[3]);
 }
 
+// q . t0 and q . t1 for two table rows in shared memory, interleaved (two independent FMA chains each).
+template <int HD>
+__device__ __forceinline__ float2 dot_rows2(const float (&q)[HD], const float* t0, const float* t1) {
+  const float4* a4 = reinterpret_cast<const float4*>(t0);
+  const float4* b4 = reinterpret_cast<const float4*>(t1);
+  float a[2] = {0.f, 0.f}, b[2] = {0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < HD / 4; ++c) {
+    const float4 u = a4[c], v = b4[c];
+    a[c & 1] = fmaf(q[4 * c], u.x, a[c & 1]);
+    b[c & 1] = fmaf(q[4 * c], v.x, b[c & 1]);
+    a[c & 1] = fmaf(q[4 * c + 1], u.y, a[c & 1]);
+    b[c & 1] = fmaf(q[4 * c + 1], v.y, b[c & 1]);
+    a[c & 1] = fmaf(q[4 * c + 2], u.z, a[c & 1]);
+    b[c & 1] = fmaf(q[4 * c + 2], v.z, b[c & 1]);
+    a[c & 1] = fmaf(q[4 * c + 3], u.w, a[c & 1]);
+    b[c & 1] = fmaf(q[4 * c + 3], v.w, b[c & 1]);
+  }
+  return make_float2(a[0] + a[1], b[0] + b[1]);
+}
+
 // Splitter of one operand (64 threads). A block = 4 source rows x 4 consecutive values: k: 4 dims x 4 keys
 // of kt [hd][n]; v: 4 keys x 4 dims of v [n][hd]. Transposed, each block gives 4 granules (4 K-values of one
 // operand row): k rows are keys (K = dims), v^T rows are dims (K = keys).
@@ -389,14 +410,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       okk = __all_sync(0xffffffffu, mbar_wait(&bars->tab_full, 0, abort_flag));
       if constexpr (G::kGlobal) {
         // rh: half hf takes kh in [32 hf, 32 hf + 32), table rows i + 63 - kh (the warp's rows share i)
-        for (int mrow = i + 32 - 32 * hf; okk && mrow <= i + 63 - 32 * hf; ++mrow)
-          srh[(i + 63 - mrow) * 128 + r] = dot_row<HD>(q, stab + mrow * HD) * kLog2e;
+        for (int mrow = i + 32 - 32 * hf; okk && mrow <= i + 63 - 32 * hf; mrow += 2) {  // 32 rows, in pairs
+          const float2 d = dot_rows2<HD>(q, stab + mrow * HD, stab + (mrow + 1) * HD);
+          srh[(i + 63 - mrow) * 128 + r] = d.x * kLog2e;
+          srh[(i + 62 - mrow) * 128 + r] = d.y * kLog2e;
+        }
         // rw of this half's keys kw in [32 hf, 32 hf + 32) (table rows j + 32 - 32 hf .. j + 63 - 32 hf) into
         // the row's own scratch
-        for (int mrow = j_lo + 32 - 32 * hf; okk && mrow <= j_hi + 63 - 32 * hf; ++mrow) {
-          const float d = dot_row<HD>(q, stab + (2 * H - 1 + mrow) * HD) * kLog2e;
+        // (63 rows in pairs: the last pair's second row, one past the range, is computed and not kept)
+        for (int mrow = j_lo + 32 - 32 * hf; okk && mrow <= j_hi + 63 - 32 * hf; mrow += 2) {
+          const float2 d = dot_rows2<HD>(q, stab + (2 * H - 1 + mrow) * HD, stab + (2 * H + mrow) * HD);
           const int kw = j + 63 - mrow;
-          if (kw >= 32 * hf && kw < 32 * hf + 32) srwtmp[kw * 128 + r] = d;
+          if (kw >= 32 * hf && kw < 32 * hf + 32) srwtmp[kw * 128 + r] = d.x * kLog2e;
+          if (kw - 1 >= 32 * hf && kw - 1 < 32 * hf + 32) srwtmp[(kw - 1) * 128 + r] = d.y * kLog2e;
         }
       } else {
         // windows: half 0 computes rh, half 1 rw; both read all of them back into registers below
