@@ -393,3 +393,31 @@ def test_empty_and_status(samrs, cuda):
     out = samrs.attention_relpos(q, torch.zeros(0, 8, 16, device=cuda), q, torch.zeros(14, 8, device=cuda), 4, 4, 1.0)
     assert out.shape == (0, 16, 8)
     assert samrs.device_status() == 0
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+@pytest.mark.parametrize("h,hd", [(14, 64), (64, 80)])
+def test_misaligned_buffers_fall_back_to_simt(samrs, cuda, h, hd, dt):
+    """q, kt, v and out one element into larger buffers (not 16-byte aligned): the tensor-core kernels need
+    16-byte alignment, so the default path takes the SIMT kernel (and matches the oracle), while forcing
+    the tensor-core path is refused with SAMRS_ERR_UNSUPPORTED."""
+    bh = 3
+    q, kt, v, t = make_inputs(h, h, bh, hd, seed=h + hd, table_std=0.5)
+
+    def offset_view(a):
+        flat = torch.zeros(a.size + 1, dtype=DT[dt], device=cuda)
+        flat[1:] = torch.from_numpy(np.ascontiguousarray(a)).reshape(-1).to(cuda).to(DT[dt])
+        return flat[1:].view(a.shape)
+
+    qd, ktd, vd = offset_view(q), offset_view(kt), offset_view(v)
+    td = to_dev(t, dt, cuda)
+    out = offset_view(np.zeros_like(q))
+    assert qd.data_ptr() % 16 != 0
+    scale = hd ** -0.5
+    samrs.attention_relpos(qd, ktd, vd, td, h, h, scale, out=out)
+    assert samrs.device_status() == 0
+    ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, h, scale)
+    assert parity_err(out.float().cpu().numpy(), ref, dt) < tol(dt)
+    with pytest.raises(samrs.SamrsError) as e:
+        samrs.attention_relpos(qd, ktd, vd, td, h, h, scale, impl="tc", out=out)
+    assert e.value.code == samrs._abi.ERR_UNSUPPORTED
