@@ -232,9 +232,54 @@ def cpu_sample(images=1, seed=7, wl=None):
     return flops / dt / 1e12, dt, desc, threads, mode
 
 
+def config1_cpu_sample(seed=7):
+    """The reference's f32 CPU path (the oracle's exact restatement of src/kernels.rs:131-225) on BASELINE
+    config 1: the windowed layer (300 heads of 14x14) and the global layer (12 heads of 64x64), hd 64."""
+    import numpy as np
+    from oracle import oracle
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    rng = np.random.default_rng(seed)
+    flops, dt = 0.0, 0.0
+    for h, bh in ((14, 300), (64, 12)):
+        n, hd = h * h, 64
+        q = rng.standard_normal((bh, n, hd), dtype=np.float32)
+        kt = rng.standard_normal((bh, hd, n), dtype=np.float32)
+        v = rng.standard_normal((bh, n, hd), dtype=np.float32)
+        t = (rng.standard_normal((4 * h - 2, hd), dtype=np.float32) * 0.5).astype(np.float32)
+        t0 = time.perf_counter()
+        oracle.attention_relpos(q, kt, v, t, h, h, hd ** -0.5, threads=threads, mode="exact")
+        dt += time.perf_counter() - t0
+        flops += layer_flops(h, h, bh, hd)
+    desc = (f"config 1 (windowed 300 heads + global 12 heads, hd 64, one image) through the f32 CPU path of "
+            f"src/kernels.rs:131-225, {threads} threads")
+    return flops / dt / 1e12, dt, desc, threads
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return 0
+    if args.config == 1:
+        for _ in range(args.warmup):
+            config1_cpu_sample()
+        vals, secs = [], []
+        desc, threads = "", 0
+        for _ in range(args.steps):
+            v, s, desc, threads = config1_cpu_sample()
+            vals.append(v)
+            secs.append(s)
+        value = statistics.median(vals)
+        line = {
+            "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(secs),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.5) rel-pos tables)",
+            "config": {"workload": "config 1: ViT-B attention op, f32, 1 image (windowed 300 heads 14x14 + global "
+                                   "12 heads 64x64, hd 64)"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
         return 0
     wl = CONFIGS[3 if args.config == 3 else 4]
     for _ in range(args.warmup):
@@ -403,6 +448,7 @@ def run_ours(args):
 
     if args.config == 1:
         c1 = run_config1(torch, samrs, device, reps=args.steps, warmup=args.warmup)
+        e2e1 = config1_e2e(torch, samrs, device, steps=args.steps, warmup=args.warmup)
         if rank == 0:
             ms = c1["layer_ms_tc"]
             flops = layer_flops(14, 14, 300, 64) + layer_flops(64, 64, 12, 64)
@@ -411,7 +457,10 @@ def run_ours(args):
                     "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                     "data": "synthetic (seeded N(0,1) activations, N(0,0.5) rel-pos tables)",
                     "config": {"workload": c1["workload"], "parallelism": f"dp{world}"},
-                    "layers": c1, "gpu_launches": 6 * args.steps}
+                    "layers": c1, "gpu_launches": 6 * args.steps, "e2e": e2e1}
+            if world == 1 and not args.no_cpu:
+                v, _, desc, threads = config1_cpu_sample()
+                line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
             print(json.dumps(line), flush=True)
         if dist is not None:
             dist.barrier()
@@ -743,6 +792,44 @@ def run_config1(torch, samrs, device, reps=20, warmup=3):
     del flush
     torch.cuda.empty_cache()
     return out
+
+
+def config1_e2e(torch, samrs, device, steps, warmup):
+    """Config 1 end to end through the library's public call: each step copies both layers' q, kt, v from
+    pinned host memory, runs the two f32 layers, and copies both outputs back (one stream, CUDA events)."""
+    g = torch.Generator().manual_seed(5)
+    layers = []
+    h2d = d2h = 0
+    for h, bh in ((14, 300), (64, 12)):
+        n, hd = h * h, 64
+        host = [torch.randn(*shape, generator=g).pin_memory() for shape in ((bh, n, hd), (bh, hd, n), (bh, n, hd))]
+        dev = [torch.empty_like(x, device=device) for x in host]
+        t = (torch.randn(4 * h - 2, hd, generator=g) * 0.5).to(device)
+        out, out_host = torch.empty_like(dev[0]), torch.empty_like(host[0]).pin_memory()
+        layers.append((h, hd, host, dev, t, out, out_host))
+        h2d += sum(x.numel() * 4 for x in host)
+        d2h += out_host.numel() * 4
+
+    def step():
+        for h, hd, host, dev, t, out, out_host in layers:
+            for d, x in zip(dev, host):
+                d.copy_(x, non_blocking=True)
+            samrs.attention_relpos(dev[0], dev[1], dev[2], t, h, h, hd ** -0.5, out=out)
+            out_host.copy_(out, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    flops = layer_flops(14, 14, 300, 64) + layer_flops(64, 64, 12, 64)
+    return {"value": flops / (ms / 1e3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": ms, "path": "samrs.attention_relpos (C ABI), pinned host buffers, one stream"}
 
 
 def run_sweep(torch, samrs, lib, device, rank, sptr, stream, dist, world, steps, warmup):
