@@ -25,6 +25,9 @@ Multi-GPU: the image batch is sharded (the per-GPU image count is fixed, weak sc
 in the data path. NCCL is used after the timed region to take the max of the per-rank device times and to
 gather per-rank output checksums.
 
+--library-context times the two attention kernels against torch SDPA on its cuDNN backend (no bias) on the
+config-4 layer shapes, with clocks and power per phase, and prints one line of its own.
+
 --impl reference times the reference's CPU implementation of the path (the C restatement under
 oracle/, the reference itself being Rust that cannot be built here) on the host cores of rank 0, on a
 bounded sample of the same workload (whole images, all layers).
@@ -178,7 +181,7 @@ class ClockSampler:
         return False
 
     def summary(self):
-        sm, smax, reasons = [], None, set()
+        sm, smax, reasons, watts = [], None, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in getattr(self, "lines", []):
             f = [x.strip() for x in line.split(",")]
@@ -189,12 +192,17 @@ class ClockSampler:
                 smax = float(f[2])
             except ValueError:
                 continue
+            try:
+                watts.append(float(f[3]))
+            except ValueError:
+                pass
             for name, val in zip(names, f[5:9]):
                 if val.lower() in ("active", "1"):
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm),
+                "power_w": statistics.median(watts) if watts else None}
 
 
 # --------------------------------------------------------------------------------------------
@@ -1044,6 +1052,85 @@ def run_e2e(args, samrs, step, device, stream, dist, world, device_ms_per_step):
             "path": "C ABI samrs_relpos_attn_fwd, pinned host buffers, upload/compute/download streams"}
 
 
+def run_library_context(args):
+    """Context for the attention kernels' rooflines: the fused rel-pos kernels against the library's plain
+    attention (torch SDPA on its cuDNN backend, no bias at all: less work than the fused op) on the same
+    shapes, one GPU. Each is run back to back for `--context-seconds` in alternating phases (ours, library,
+    ours, library) with nvidia-smi sampled during each phase, so that the two are compared at the clocks the
+    power cap leaves each of them. Prints one JSON line ("impl": "library-context")."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    samrs = importlib.import_module("sam-rs_b200")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peaks = load_peaks()
+    g = torch.Generator(device=device).manual_seed(11)
+    images, heads, hd = 32, VIT_H["heads"], VIT_H["hd"]
+
+    def phase(fn, secs):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        with ClockSampler(0) as clk:
+            t0 = time.time()
+            while time.time() - t0 < secs:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(5):
+                    fn()
+                b.record()
+                b.synchronize()
+                times.append(a.elapsed_time(b) / 5)
+        c = clk.summary()
+        ms = statistics.median(times)
+        return {"ms": ms, "min_ms": min(times), "launches": 5 * len(times), "sm_mhz": c["sm_mhz"],
+                "power_w": c["power_w"], "reasons": c["reasons"],
+                "mcycles_per_launch": ms * c["sm_mhz"] / 1e3 if c["sm_mhz"] else None}
+
+    out = {"impl": "library-context", "n_gpus": 1, "dtype": "bf16", "data": "synthetic (seeded N(0,1), tables N(0,0.5))",
+           "library": f"torch {torch.__version__} scaled_dot_product_attention, cuDNN backend "
+                      f"{torch.backends.cudnn.version()}, no bias",
+           "peaks": {"hbm_gbs": peaks[0], "bf16_burst_tflops": peaks[1], "bf16_sustained_tflops": peaks[2],
+                     "source": peaks[3]}, "layers": {}}
+    for kind, side, bh in (("global", 64, images * heads), ("window", 14, images * 25 * heads)):
+        n = side * side
+        q = torch.randn(bh, n, hd, device=device, generator=g).bfloat16()
+        kt = torch.randn(bh, hd, n, device=device, generator=g).bfloat16()
+        v = torch.randn(bh, n, hd, device=device, generator=g).bfloat16()
+        t = (torch.randn(4 * side - 2, hd, device=device, generator=g) * 0.5).bfloat16()
+        b = bh // heads
+        q4, v4 = q.view(b, heads, n, hd), v.view(b, heads, n, hd)
+        k4 = kt.view(b, heads, hd, n).transpose(2, 3).contiguous()
+
+        def ours():
+            samrs.attention_relpos(q, kt, v, t, side, side, hd ** -0.5, impl="tc")
+
+        def library():
+            with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+                F.scaled_dot_product_attention(q4, k4, v4)
+
+        flops, nbytes = layer_flops(side, side, bh, hd), layer_bytes(side, side, bh, hd)
+        res = {"bh": bh, "tokens": n, "hd": hd, "gflop": flops / 1e9, "algorithmic_mb": nbytes / 1e6}
+        for rnd in range(2):
+            for name, fn in (("fused_relpos", ours), ("cudnn_sdpa_no_bias", library)):
+                try:
+                    r = phase(fn, args.context_seconds)
+                except RuntimeError as e:
+                    r = {"unavailable": str(e).splitlines()[0][:160]}
+                if "ms" in r:
+                    r["tflops"] = flops / r["ms"] / 1e9
+                    r["gbs"] = nbytes / r["ms"] / 1e6
+                res.setdefault(name, []).append(r)
+        out["layers"][kind] = res
+        del q, kt, v, q4, k4, v4
+        torch.cuda.empty_cache()
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -1057,7 +1144,12 @@ def main(argv=None):
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip configs 3 and 5 in the default config-4 run")
     ap.add_argument("--no-neighbours", action="store_true", help="skip timing the qkv split / head merge kernels")
+    ap.add_argument("--library-context", action="store_true",
+                    help="time the attention kernels against torch SDPA (cuDNN, no bias) on the same shapes")
+    ap.add_argument("--context-seconds", type=float, default=6.0)
     args = ap.parse_args(argv)
+    if args.library_context:
+        return run_library_context(args)
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
