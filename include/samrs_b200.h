@@ -210,6 +210,21 @@ SAMRS_API int samrs_test_hooks(int64_t wait_limit_cycles, int withhold_key_tile)
 SAMRS_API int samrs_recompute_count(void* stream, int64_t* count, int clear);
 
 /*
+ * The per-layer choice for bf16 global layers on the current device. A layer is keyed by the address of its
+ * rel-pos table. The speculative pass plus the fixup launch is kept while the measured share of CTAs that
+ * the fixup recomputes stays at or below 0.15. Above that, the layer runs the exact two-pass kernel alone
+ * for its next 32 calls, and is then measured again. The speculative pass costs 0.87x the exact kernel, and
+ * each recomputed CTA costs an exact CTA on top of it.
+ * A measurement is read back without waiting: it takes effect from the first call after its own call has
+ * completed on the device.
+ * Writes the layer's last measured share (-1 if never measured) to `share`, and to `exact` whether its next
+ * call launches the exact kernel. `reset` != 0 first forgets every layer's history, so each layer's next call
+ * measures again. Does not synchronise (a measurement still in flight is simply not read yet).
+ * No counterpart in the reference (its kernels have no speculative pass).
+ */
+SAMRS_API int samrs_global_policy(const void* table, double* share, int* exact, int reset);
+
+/*
  * Self-test hook of the library's own exp2 polynomial (the FMA-pipe exponential the windowed kernel uses
  * for one key pair in eight): y_poly[i] = the polynomial at x[i], y_lib[i] = CUDA's exp2f(x[i]); device
  * f32 buffers of n elements. Test infrastructure; no counterpart in the reference.

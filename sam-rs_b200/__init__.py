@@ -30,7 +30,7 @@ from ._abi import SamrsError
 
 __all__ = ["relpos_softmax", "attention_relpos", "attention_relpos_cpu", "qkv_split", "qkv_split_window",
            "window_merge", "bmm", "Attention", "window_partition", "window_unpartition", "device_status",
-           "recompute_count", "linear", "qkv_linear_window", "layer_norm", "Block", "SamrsError"]
+           "recompute_count", "global_policy", "linear", "qkv_linear_window", "layer_norm", "Block", "SamrsError"]
 
 _DTYPES = {torch.float32: _abi.F32, torch.float16: _abi.F16, torch.bfloat16: _abi.BF16}
 _IMPLS = {"auto": _abi.IMPL_AUTO, "simt": _abi.IMPL_SIMT, "tc": _abi.IMPL_TC}
@@ -238,6 +238,16 @@ def recompute_count(clear=True):
     n = ctypes.c_int64(0)
     _abi.check(_abi.lib().samrs_recompute_count(_stream(), ctypes.byref(n), 1 if clear else 0))
     return int(n.value)
+
+
+def global_policy(table, reset=False):
+    """The library's choice for the bf16 global layer whose rel-pos table is `table`: (last measured share of
+    CTAs the exact second pass recomputed, -1 if none; True if its next call runs the exact kernel alone).
+    reset=True first forgets every layer's history on the current device."""
+    share, exact = ctypes.c_double(0.0), ctypes.c_int(0)
+    _abi.check(_abi.lib().samrs_global_policy(ctypes.c_void_p(table.data_ptr()), ctypes.byref(share),
+                                              ctypes.byref(exact), 1 if reset else 0))
+    return float(share.value), bool(exact.value)
 
 
 def window_partition(x, ws):

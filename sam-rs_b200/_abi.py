@@ -55,11 +55,12 @@ def lib():
         l.samrs_device_status.argtypes = [vp, i32]
         l.samrs_recompute_count.argtypes = [vp, ctypes.POINTER(i64), i32]
         l.samrs_selftest_ex2.argtypes = [vp, vp, vp, i64, vp]
+        l.samrs_global_policy.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i32), i32]
         for name in ("samrs_relpos_attn_fwd", "samrs_relpos_attn_fwd_ex", "samrs_relpos_softmax_fwd",
                      "samrs_qkv_split_fwd", "samrs_qkv_split_window_fwd", "samrs_window_merge_fwd",
                      "samrs_abi_version", "samrs_device_status", "samrs_recompute_count",
                      "samrs_selftest_ex2", "samrs_linear_fwd", "samrs_qkv_linear_window_fwd",
-                     "samrs_layer_norm_fwd", "samrs_test_hooks"):
+                     "samrs_layer_norm_fwd", "samrs_test_hooks", "samrs_global_policy"):
             getattr(l, name).restype = i32
         _lib = l
     return _lib

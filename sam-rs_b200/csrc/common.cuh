@@ -33,6 +33,11 @@ __device__ int g_withhold_key_tile = -1;
 // read and cleared by samrs_recompute_count(). A statistic for the caller, not read by any kernel.
 __device__ unsigned long long g_recomputed = 0;
 
+// Per-layer recompute counters of the host's speculative-pass policy (global_policy.h): a measuring call
+// zeroes its layer's slot on its stream and points the fixup launch at it. No kernel reads them.
+constexpr int kPolicySlots = 64;
+__device__ unsigned long long g_policy_counts[kPolicySlots];
+
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }

@@ -6,6 +6,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "global_policy.h"
 #include "relpos_tc_f32.cuh"
 #include "relpos_tc_global.cuh"
 #include "relpos_tc_window.cuh"
@@ -98,19 +99,32 @@ int tc_launch_global(const void* q, const void* kt, const void* v, const void* t
   if (!rc) rc = make_map(&mt, bf16, table, HD, 4 * kSide - 2, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
   // f16: the exact kernel. bf16: the speculative kernel, then the fixup launch, which recomputes exactly
-  // the CTAs the first one marked (the others return at once).
+  // the CTAs the first one marked (the others return at once); or, for a layer whose measured recompute
+  // share made the speculative pass the slower choice (global_policy.h), the exact kernel alone.
+  auto exact = relpos_attn_global<T, HD, kModeExact>;
   auto first = relpos_attn_global<T, HD, bf16 ? kModeSpec : kModeExact>;
   auto fixup = relpos_attn_global<T, HD, bf16 ? kModeFixup : kModeExact>;
   const int split = 128 * kRegsLow + 512 * kRegsHigh;
-  static const bool regs_ok = regs_cover_split(first, kThreads, split) && regs_cover_split(fixup, kThreads, split);
+  static const bool regs_ok = regs_cover_split(exact, kThreads, split) && regs_cover_split(first, kThreads, split) &&
+                              regs_cover_split(fixup, kThreads, split);
   if (!regs_ok) return 6;
   const int smem = Layout<HD>::kSmemBytes;
-  if (cudaFuncSetAttribute(first, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+  if (cudaFuncSetAttribute(exact, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaFuncSetAttribute(first, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
       cudaFuncSetAttribute(fixup, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return 5;
   const unsigned grid = (unsigned)(bh * (kN / 256));
-  first<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale);
-  if (bf16) fixup<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale);
+  GlobalPolicy::Choice ch;
+  ch.exact = !bf16;
+  int dev = -1;
+  if (bf16 && cudaGetDevice(&dev) == cudaSuccess) ch = global_policy().choose(dev, table, grid, st);
+  if (ch.exact) {
+    exact<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale, nullptr);
+    return 0;
+  }
+  first<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale, nullptr);
+  fixup<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale, ch.slot);
+  global_policy().after_launch(dev, ch, st);
   return 0;
 }
 

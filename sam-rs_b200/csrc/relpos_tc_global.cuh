@@ -224,7 +224,7 @@ template <typename T, int HD, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     relpos_attn_global(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmT,
-                       T* __restrict__ out, float scale) {
+                       T* __restrict__ out, float scale, unsigned long long* recompute_slot) {
   using L = Layout<HD>;
   using namespace sm100;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -252,7 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (MODE == kModeFixup) {
         const float m = to_f(*reinterpret_cast<volatile T*>(marker));
         skip |= !(m != m);
-        if (!skip) atomicAdd(&g_recomputed, 1ull);
+        if (!skip) {
+          atomicAdd(&g_recomputed, 1ull);
+          if (recompute_slot) atomicAdd(recompute_slot, 1ull);  // the host's per-layer measurement
+        }
       }
     }
     if (__syncthreads_or(skip)) return;

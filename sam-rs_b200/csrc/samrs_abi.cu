@@ -596,6 +596,15 @@ int samrs_recompute_count(void* stream, int64_t* count, int clear) {
   return ok();
 }
 
+int samrs_global_policy(const void* table, double* share, int* exact, int reset) {
+  if (!share || !exact) return fail(SAMRS_ERR_INVALID, "global_policy: null output pointer");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(SAMRS_ERR_NODEVICE, "no CUDA device is current");
+  if (reset) global_policy().reset(dev);
+  global_policy().state(dev, table, share, exact);
+  return ok();
+}
+
 int samrs_selftest_ex2(const void* x, void* y_poly, void* y_lib, int64_t n, void* stream) {
   if (n < 0 || n > ((int64_t)1 << 30)) return fail(SAMRS_ERR_INVALID, "selftest_ex2: n = %lld", (long long)n);
   if (n == 0) return ok();

@@ -18,7 +18,8 @@ def test_library_exports_every_header_symbol():
                           "samrs_qkv_split_fwd", "samrs_qkv_split_window_fwd", "samrs_window_merge_fwd",
                           "samrs_last_error", "samrs_abi_version", "samrs_device_status",
                           "samrs_recompute_count", "samrs_selftest_ex2", "samrs_linear_fwd",
-                          "samrs_qkv_linear_window_fwd", "samrs_layer_norm_fwd", "samrs_test_hooks"}
+                          "samrs_qkv_linear_window_fwd", "samrs_layer_norm_fwd", "samrs_test_hooks",
+                          "samrs_global_policy"}
     lib = ctypes.CDLL(a.LIB_PATH)
     for n in names:
         assert hasattr(lib, n), n
@@ -49,6 +50,7 @@ def test_null_pointers_rejected():
     a = abi()
     assert a.lib().samrs_relpos_attn_fwd(0, 0, 0, 0, 0, 1, 4, 4, 8, 0.5, 0, None) == -1
     assert a.lib().samrs_recompute_count(None, None, 0) == -1
+    assert a.lib().samrs_global_policy(None, None, None, 0) == -1
     assert a.lib().samrs_selftest_ex2(0, 0, 0, 4, None) == -1
     assert a.lib().samrs_selftest_ex2(0, 0, 0, -1, None) == -1
     assert a.lib().samrs_selftest_ex2(0, 0, 0, 0, None) == 0

@@ -145,6 +145,7 @@ def test_global_late_max_jumps(samrs, cuda, hd, dt):
             kt[b, 0, key] = big
     scale = hd ** -0.5
     qd, ktd, vd, td = (to_dev(x, dt, cuda) for x in (q, kt, v, t))
+    samrs.global_policy(td, reset=True)  # bf16: the speculative pass and its fixup, whatever ran before
     out = samrs.attention_relpos(qd, ktd, vd, td, h, w, scale)
     assert samrs.device_status() == 0
     ref = oracle.attention_relpos(rounded(qd), rounded(ktd), rounded(vd), rounded(td), h, w, scale)
@@ -216,6 +217,7 @@ def test_global_bf16_overflow_recompute(samrs, cuda, hd):
     kt[1, 0, 128 * 30 + 101] = 40.0
     scale = hd ** -0.5
     qd, ktd, vd, td = (to_dev(x, "bf16", cuda) for x in (q, kt, v, t))
+    samrs.global_policy(td, reset=True)
     out = samrs.attention_relpos(qd, ktd, vd, td, h, w, scale)
     assert samrs.device_status() == 0
     got = out.float().cpu().numpy()
@@ -230,15 +232,64 @@ def test_bf16_recompute_counter(samrs, cuda):
     overflow case above marks some CTAs (one head x 256 rows each) and the counter sees them."""
     samrs.recompute_count(clear=True)
     q, kt, v, t = make_inputs(64, 64, 4, 80, seed=3, table_std=0.5)
-    samrs.attention_relpos(*(to_dev(x, "bf16", cuda) for x in (q, kt, v, t)), 64, 64, 80 ** -0.5)
+    args = [to_dev(x, "bf16", cuda) for x in (q, kt, v, t)]
+    samrs.global_policy(args[3], reset=True)
+    samrs.attention_relpos(*args, 64, 64, 80 ** -0.5)
     assert samrs.recompute_count() == 0
     q, kt, v, t = make_inputs(64, 64, 2, 80, seed=91, table_std=0.5)
     q[:, :, 0] = 4.0
     v *= 1e35
     kt[0, 0, 128 * 5 + 17] = 40.0
-    samrs.attention_relpos(*(to_dev(x, "bf16", cuda) for x in (q, kt, v, t)), 64, 64, 80 ** -0.5)
+    args = [to_dev(x, "bf16", cuda) for x in (q, kt, v, t)]
+    samrs.global_policy(args[3], reset=True)
+    samrs.attention_relpos(*args, 64, 64, 80 ** -0.5)
     assert samrs.device_status() == 0
     assert 1 <= samrs.recompute_count() <= 2 * 16
+
+
+def test_global_bf16_policy_switches_to_exact(samrs, cuda):
+    """A bf16 global layer whose CTAs mostly need the exact second pass (activations and rel-pos table of
+    std 2: rel-pos bias spreads of hundreds of log2 units) is switched to the exact kernel alone once its
+    measured recompute share is read back, returns to the speculative pass (measured again) after 32 exact
+    calls, and stays speculative on ordinary data. Every output matches the oracle on sampled heads."""
+    h = w = 64
+    hd, bh = 80, 16
+    q, kt, v, t = make_inputs(h, w, bh, hd, seed=123, table_std=2.0)
+    q *= 2.0
+    kt *= 2.0
+    scale = hd ** -0.5
+    qd, ktd, vd, td = (to_dev(x, "bf16", cuda) for x in (q, kt, v, t))
+    heads = [0, 7, 15]
+    ref = oracle.attention_relpos(rounded(qd)[heads], rounded(ktd)[heads], rounded(vd)[heads], rounded(td), h, w,
+                                  scale)
+
+    def run():
+        out = samrs.attention_relpos(qd, ktd, vd, td, h, w, scale)
+        assert samrs.device_status() == 0
+        err = parity_err(out.float().cpu().numpy()[heads], ref, "bf16")
+        assert err < HALF_TOL, err
+
+    share, exact = samrs.global_policy(td, reset=True)
+    assert (share, exact) == (-1.0, False)
+    samrs.recompute_count(clear=True)
+    run()  # speculative pass + fixup, measured
+    recomputed = samrs.recompute_count(clear=True)
+    share, exact = samrs.global_policy(td)
+    assert share == recomputed / (bh * 16) and share > 0.15 and exact, (share, recomputed)
+    for _ in range(32):
+        run()  # the exact kernel alone: nothing for the fixup to count
+    assert samrs.recompute_count(clear=True) == 0
+    share2, exact2 = samrs.global_policy(td)
+    assert not exact2 and share2 == share
+    run()  # the probe: speculative again, measured again
+    assert samrs.recompute_count(clear=True) == recomputed
+    assert samrs.global_policy(td) == (share, True)
+    # ordinary data (N(0,1) activations, N(0, 0.5) table) on its own table: measured, kept speculative
+    q, kt, v, t = make_inputs(h, w, 4, hd, seed=124, table_std=0.5)
+    args = [to_dev(x, "bf16", cuda) for x in (q, kt, v, t)]
+    samrs.attention_relpos(*args, h, w, scale)
+    assert samrs.recompute_count(clear=True) == 0
+    assert samrs.global_policy(args[3]) == (0.0, False)
 
 
 def test_ex2_polynomial_against_cuda_exp2f(samrs, cuda):
