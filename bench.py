@@ -28,6 +28,9 @@ gather per-rank output checksums.
 --library-context times the two attention kernels against torch SDPA on its cuDNN backend (no bias) on the
 config-4 layer shapes, with clocks and power per phase, and prints one line of its own.
 
+--impl reference --reference-path cuda times the reference's own CUDA path on the GPU instead (its
+kernels/sam.cu relpos_softmax between cuBLAS bmm's, compiled into oracle/_ref), on the same workload.
+
 --impl reference times the reference's CPU implementation of the path (the C restatement under
 oracle/, the reference itself being Rust that cannot be built here) on the host cores of rank 0, on a
 bounded sample of the same workload (whole images, all layers).
@@ -263,10 +266,74 @@ def config1_cpu_sample(seed=7):
     return flops / dt / 1e12, dt, desc, threads
 
 
+def run_reference_cuda(args):
+    """The reference's own CUDA path on this GPU: bmm(relpos_softmax(bmm(q, kt)), v) per layer
+    (src/sam1/encoder.rs:81). Its kernels/sam.cu is compiled into oracle/_ref by oracle/build_ref_cuda.py and
+    launched as the reference launches it; the bmm's are cuBLAS in the I/O dtype with f32 accumulation, as
+    candle's are. Same workload, inputs resident in HBM, CUDA events around K steps."""
+    import torch
+    from oracle.ref_cuda import RefCuda, RefCudaError
+    wl = CONFIGS[3 if args.config == 3 else 4]
+    images = args.images or wl.images
+    try:
+        ref = RefCuda()
+    except (RefCudaError, OSError) as e:
+        print(json.dumps({"impl": "reference", "reference_path": "cuda", "unavailable": str(e)}), flush=True)
+        return 0
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device).manual_seed(1234)
+    sets = {}
+    for kind in KINDS:
+        _, h, w, bh = next(x for x in layer_geoms(images, wl) if x[0] == kind)
+        n = h * w
+        sets[kind] = (h, w, torch.randn(bh, n, wl.hd, device=device, generator=g).bfloat16(),
+                      torch.randn(bh, wl.hd, n, device=device, generator=g).bfloat16(),
+                      torch.randn(bh, n, wl.hd, device=device, generator=g).bfloat16(),
+                      (torch.randn(4 * h - 2, wl.hd, device=device, generator=g) * 0.5).bfloat16())
+    geoms = layer_geoms(images, wl)
+    scale = wl.hd ** -0.5
+
+    def step():
+        for kind, *_ in geoms:
+            h, w, q, kt, v, t = sets[kind]
+            ref.attention(q, kt, v, t, h, w, scale)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        b.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    flops = sum(layer_flops(h, w, bh, wl.hd) for _, h, w, bh in geoms)
+    value = flops / (ms / 1e3) / 1e12
+    line = {
+        "impl": "reference", "reference_path": "cuda", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.5) rel-pos tables)",
+        "config": {"workload": f"config {3 if args.config == 3 else 4}: " + wl.describe(), "images_per_gpu": images,
+                   "path": "the reference's CUDA path: cuBLAS bmm (I/O dtype, f32 accumulation), its "
+                           "relpos_softmax kernel (kernels/sam.cu, built with its own nvcc flags), cuBLAS bmm; "
+                           "inputs resident in HBM"},
+        "images_per_s": images / (ms / 1e3),
+        "clocks": clk.summary(),
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    if args.reference_path == "cuda":
+        return run_reference_cuda(args)
     if args.config == 1:
         for _ in range(args.warmup):
             config1_cpu_sample()
@@ -1166,6 +1233,9 @@ def main(argv=None):
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip configs 3 and 5 in the default config-4 run")
     ap.add_argument("--no-neighbours", action="store_true", help="skip timing the qkv split / head merge kernels")
+    ap.add_argument("--reference-path", choices=["cpu", "cuda"], default="cpu",
+                    help="with --impl reference: the reference's CPU path (default; the oracle's restatement) or "
+                         "its own CUDA kernels (oracle/_ref, built from its kernels/sam.cu) on this GPU")
     ap.add_argument("--library-context", action="store_true",
                     help="time the attention kernels against torch SDPA (cuDNN, no bias) on the same shapes")
     ap.add_argument("--context-seconds", type=float, default=6.0)

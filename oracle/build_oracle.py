@@ -2,8 +2,9 @@
 
     python oracle/build_oracle.py      -> oracle/liboracle.so
 
-The reference (apiplant/sam-rs) is Rust and cannot be compiled here (no cargo/rustc), so there is no
-oracle/_ref build; the oracle is the C restatement in relpos_oracle.c.
+The reference (apiplant/sam-rs) is Rust and its CPU path cannot be compiled here (no cargo/rustc); the
+oracle is the C restatement in relpos_oracle.c. The reference's CUDA kernels are plain CUDA C and are
+compiled by build_ref_cuda.py into oracle/_ref/ (the parity tests run them).
 """
 import os
 import subprocess
