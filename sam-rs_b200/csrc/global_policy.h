@@ -12,7 +12,8 @@
 // A later call on the same layer reads it once the event has completed, and never waits for it. The
 // first call on a layer and every kMeasureEvery-th speculative call measure. Above kExactShare the layer
 // switches to the exact kernel for kExactCalls calls, after which the speculative pass is tried (and
-// measured) again. A stream that is capturing a CUDA graph only replays the current choice.
+// measured) again. A stream that is capturing a CUDA graph replays the current choice: no measurement,
+// no event query, and the exact-call count does not advance.
 // No counterpart in the reference (its kernels have no speculative pass).
 #pragma once
 #include <cuda_runtime.h>
@@ -47,20 +48,28 @@ class GlobalPolicy {
     if (dev < 0 || dev >= kMaxDevices) return c;
     Dev& d = devs_[dev];
     std::lock_guard<std::mutex> lock(d.mu);
-    if (!d.ready && !init(d, dev)) return c;
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    const bool capturing = cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone;
+    const cudaError_t ce = cudaStreamIsCapturing(st, &cs);
+    if (ce != cudaSuccess) (void)cudaGetLastError();
+    if (ce != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+      // Inside a graph capture: replay the layer's current choice. No set-up, event query, copy or counter
+      // update (such calls are not allowed while a stream captures in the global mode).
+      const int i = d.ready ? find(d, table) : -1;
+      c.exact = i >= 0 && d.entries[i].exact_left > 0;
+      return c;
+    }
+    if (!d.ready && !init(d, dev)) return c;
     const int i = find_or_claim(d, table);
     if (i < 0) return c;  // every slot this table may use has a read-back in flight: no measurement
     Entry& e = d.entries[i];
     e.last_use = ++d.clock;
     consume(d, i);
     if (e.exact_left > 0) {
-      if (!capturing && --e.exact_left == 0) e.since_measure = kMeasureEvery;  // probe on the next call
+      if (--e.exact_left == 0) e.since_measure = kMeasureEvery;  // probe on the next call
       c.exact = true;
       return c;
     }
-    if (capturing || e.pending) return c;
+    if (e.pending) return c;
     if (++e.since_measure < kMeasureEvery) return c;
     e.since_measure = 0;
     if (cudaMemsetAsync(d.dev_slots + i, 0, sizeof(unsigned long long), st) != cudaSuccess) {

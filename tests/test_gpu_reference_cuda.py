@@ -165,3 +165,29 @@ def test_reference_cuda_attention_path(samrs, cuda, ref, h, w, bh, hd, dt):
     else:
         assert parity_err(host(fused), exact, dt) < HALF_TOL
         assert e_fused <= max(e_path, HALF_TOL + ROUNDING_SLACK[dt]), (e_fused, e_path)
+
+
+GOLDEN = sorted(__import__("glob").glob(os.path.join(os.path.dirname(__file__), "golden", "golden_*.npz")))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=os.path.basename)
+def test_golden_fixtures_vs_reference_kernels(cuda, ref, path):
+    """The committed golden fixtures (float64 restatement of the reference's tensor-op fallback) against the
+    reference's own CUDA code in f32: its attention path for the stored output rows, its relpos_softmax
+    kernel for the stored probability rows (scores rounded to f16 as the fixture's softmax KAT does)."""
+    from tests.golden.make_golden import digest, f16_round, make_inputs as golden_inputs
+    g = np.load(path)
+    h, w, bh, hd, seed = (int(g[k]) for k in ("h", "w", "bh", "hd", "seed"))
+    scale = float(g["scale"])
+    q, kt, v, t = golden_inputs(h, w, bh, hd, seed)
+    assert digest(q, kt, v, t) == str(g["input_sha256"])
+    qd, ktd, vd, td = (dev(x, "f32", cuda) for x in (q, kt, v, t))
+    out = host(ref.attention(qd, ktd, vd, td, h, w, scale))[:, g["rows"], :]
+    e_out = rel_max_err(out, g["out_rows"])
+    s16 = torch.from_numpy(f16_round(np.matmul(q.astype(np.float64), kt.astype(np.float64)).astype(np.float32)))
+    probs = host(ref.relpos_softmax(s16.to(cuda).contiguous(), qd, td, h, w, scale))[:, g["probs_row_ids"], :]
+    e_p = float(np.abs(probs - g["probs_rows"]).max())
+    print(f"{os.path.basename(path)}: reference CUDA path vs fixture {e_out:.2e} (relative), reference softmax "
+          f"kernel vs fixture {e_p:.2e} (abs)")
+    assert e_out < 1e-5, e_out
+    assert e_p < 1e-5, e_p
