@@ -17,6 +17,7 @@
 #include "layernorm.cuh"
 #include "relpos_tc.cuh"
 #include "window_io.cuh"
+#include "window_tma.cuh"
 
 namespace {
 
@@ -188,6 +189,29 @@ int launch_split_window(const void* y, const void* bias, void* out, int64_t imag
   else
     kone<<<grid, 256, smem, st>>>(yp, bp, op, (long)units, g);
   return launch_status("qkv_split_window");
+}
+
+// The windowed layers' split and merge as TMA tile moves (window_tma.cuh) where a (window, head) block moves
+// as one box; the vectorised / scalar kernels of window_io.cuh otherwise (global layers, odd head dims,
+// unaligned buffers). Both give the same bits.
+template <typename T>
+int split_window_any(const void* y, const void* bias, void* out, int64_t images, const WinGeom& g, bool windowed,
+                     cudaStream_t st) {
+  if (wtma::tma_window_ok<T>(g, windowed, 1, y, bias, out) &&
+      wtma::launch_split_window_tma<T>(y, bias, out, images, g, st) == 0)
+    return launch_status("qkv_split_window");
+  return launch_split_window<T>(y, bias, out, images, g, st);
+}
+
+template <typename T>
+int launch_merge(const void* attn, void* out, int64_t images, const WinGeom& g, int num_sms, cudaStream_t st);
+
+template <typename T>
+int merge_any(const void* attn, void* out, int64_t images, const WinGeom& g, bool windowed, int num_sms,
+              cudaStream_t st) {
+  if (wtma::tma_window_ok<T>(g, windowed, 1, attn, out, out) && wtma::launch_merge_tma<T>(attn, out, images, g, st) == 0)
+    return launch_status("window_merge");
+  return launch_merge<T>(attn, out, images, g, num_sms, st);
 }
 
 template <typename T>
@@ -422,11 +446,11 @@ int samrs_qkv_split_window_fwd(const void* y, const void* bias, void* out, int64
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case SAMRS_F32:
-      return launch_split_window<float>(y, bias, out, images, g, st);
+      return split_window_any<float>(y, bias, out, images, g, ws > 0, st);
     case SAMRS_F16:
-      return launch_split_window<__half>(y, bias, out, images, g, st);
+      return split_window_any<__half>(y, bias, out, images, g, ws > 0, st);
     default:
-      return launch_split_window<__nv_bfloat16>(y, bias, out, images, g, st);
+      return split_window_any<__nv_bfloat16>(y, bias, out, images, g, ws > 0, st);
   }
 }
 
@@ -445,11 +469,11 @@ int samrs_window_merge_fwd(const void* attn, void* out, int64_t images, int h, i
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case SAMRS_F32:
-      return launch_merge<float>(attn, out, images, g, dev->num_sms, st);
+      return merge_any<float>(attn, out, images, g, ws > 0, dev->num_sms, st);
     case SAMRS_F16:
-      return launch_merge<__half>(attn, out, images, g, dev->num_sms, st);
+      return merge_any<__half>(attn, out, images, g, ws > 0, dev->num_sms, st);
     default:
-      return launch_merge<__nv_bfloat16>(attn, out, images, g, dev->num_sms, st);
+      return merge_any<__nv_bfloat16>(attn, out, images, g, ws > 0, dev->num_sms, st);
   }
 }
 

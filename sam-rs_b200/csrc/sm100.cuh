@@ -112,10 +112,27 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// ------------------------------------------------------------------- non-bulk async copies
-// 8-byte global -> shared copy (both addresses 8-byte aligned), completion via cp_async_wait_all.
-// Bulk (non-tensor) store shared -> global, tracked by this thread's bulk groups. Both addresses 16-byte
-// aligned, size a multiple of 16.
+// 4-D tiled bulk tensor load global -> shared (coordinates innermost first); elements outside the tensor
+// are zero-filled (the maps are encoded with OOB fill NONE). No multicast.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// 4-D tiled bulk tensor store shared -> global, tracked by this thread's bulk groups. Box elements outside
+// the tensor are not written. Coordinates must not be negative.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
+// ------------------------------------------------------------------- bulk and non-bulk async copies
 // Bulk (non-tensor) load global -> shared of this CTA, completion counted on `bar` (bytes). Both addresses
 // 16-byte aligned, size a multiple of 16. No multicast.
 __device__ __forceinline__ void bulk_load(void* sdst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
@@ -125,6 +142,8 @@ __device__ __forceinline__ void bulk_load(void* sdst, const void* gsrc, uint32_t
                : "memory");
 }
 
+// Bulk (non-tensor) store shared -> global, tracked by this thread's bulk groups. Both addresses 16-byte
+// aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
                "r"(bytes)
@@ -136,6 +155,7 @@ __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.w
 // Waits until this thread's bulk stores have completed.
 __device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// 8-byte global -> shared copy (both addresses 8-byte aligned), completion via cp_async_wait_all.
 __device__ __forceinline__ void cp_async_8(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }

@@ -380,8 +380,11 @@ def test_attention_block_chain(samrs, cuda):
     assert rel_max_err(y.reshape(-1, c).cpu().numpy(), ref.numpy()) < 1e-3
 
 
-WIN_GEOMS = [(2, 64, 64, 14, 16, 80), (2, 13, 20, 7, 3, 24), (1, 16, 16, 0, 4, 32), (1, 14, 14, 14, 2, 16),
-             (1, 9, 11, 4, 2, 12)]
+# ViT-H / ViT-B windowed (TMA path), pads along both axes with an odd window token count (vectorised
+# path), global (one window), exact fit (TMA), ragged on both axes (TMA: zero-filled loads, clipped
+# stores), hd 12 (scalar path in 16-bit, TMA in f32)
+WIN_GEOMS = [(2, 64, 64, 14, 16, 80), (1, 64, 64, 14, 12, 64), (2, 13, 20, 7, 3, 24), (1, 16, 16, 0, 4, 32),
+             (1, 14, 14, 14, 2, 16), (2, 30, 20, 8, 4, 32), (1, 9, 11, 4, 2, 12)]
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
