@@ -6,8 +6,9 @@
 //
 // These layers are HBM-bound (~98 FLOP/B at hd 80), so the kernel streams: a persistent grid (one CTA
 // per SM) walks over units = (window, head) pairs with the loads of later units in flight. Per unit the
-// 196 query rows are two 128-row MMA tiles and all keys fit one key tile, so the softmax is a plain
-// two-pass row softmax (no online rescaling).
+// 196 query rows are two 128-row MMA tiles and all keys fit one key tile, so each row's softmax sees all
+// its keys at once: f16 takes the exact row max in a first pass over S; bf16 takes a single pass with the
+// reference from the row's first 32 keys (row_exp_online).
 //
 // One N = 256 MMA per tile yields scores and bias projections together: the B operand holds the 196
 // keys followed by the 27 rows of rel_pos_h and the 27 rows of rel_pos_w (196 + 54 = 250 <= 256), so
@@ -200,49 +201,6 @@ __device__ __forceinline__ float row_max(uint32_t tS, float2 c2, const Bias& b) 
   return max3(max3(m[0], m[1], m[2]), max3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 
-// Max of the raw scores S over the 196 keys of chunk CH (8 independent maxima).
-template <int CH>
-__device__ __forceinline__ void chunk_smax(const uint32_t (&sv)[32], float (&m)[8]) {
-#pragma unroll
-  for (int e = 0; e < 32; e += 2)
-    if (32 * CH + e < kN) m[(e >> 1) & 7] = sm100::max3(m[(e >> 1) & 7], __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
-}
-
-// Upper bound of the row max for bf16: c * max S + max rh + max rw (log2 units). It exceeds the true max
-// by at most the row's rh and rw spreads; any reference at or above the max gives the same softmax once the
-// row sums come from the rounded P (the ones block), and bf16 P holds 2^-126 .. 2^127. One max per key pair
-// instead of the exact pass's fma, add and max.
-__device__ __forceinline__ float row_max_bound(uint32_t tS, float c, float rhm, float rwm) {
-  using namespace sm100;
-  uint32_t a[32], bb[32], a2[32], bb2[32];
-  float m[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = -INFINITY;
-  tmem_ld32(tS + 0, a);
-  tmem_ld32(tS + 32, bb);
-  tmem_wait_ld_regs(a);
-  tmem_wait_ld_regs(bb);
-  tmem_ld32(tS + 64, a2);
-  tmem_ld32(tS + 96, bb2);
-  chunk_smax<0>(a, m);
-  chunk_smax<1>(bb, m);
-  tmem_wait_ld_regs(a2);
-  tmem_wait_ld_regs(bb2);
-  tmem_ld32(tS + 128, a);
-  tmem_ld32(tS + 160, bb);
-  chunk_smax<2>(a2, m);
-  chunk_smax<3>(bb2, m);
-  tmem_wait_ld_regs(a);
-  tmem_wait_ld_regs(bb);
-  tmem_ld32(tS + 192, a2);  // columns 192..223: keys 192..195
-  chunk_smax<4>(a, m);
-  chunk_smax<5>(bb, m);
-  tmem_wait_ld_regs(a2);
-  chunk_smax<6>(a2, m);
-  const float ms = max3(max3(m[0], m[1], m[2]), max3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
-  return ms * c + rhm + rwm;
-}
-
 // p = 2^(x - m) for all keys (the bias pairs already hold rw - m), P written as 16-bit pairs over the
 // consumed S columns 0..103. The load of chunk k+1 is in flight while chunk k is exponentiated.
 template <bool BF16>
@@ -276,6 +234,156 @@ __device__ __forceinline__ void row_exp(uint32_t tS, float2 c2, const Bias& b) {
   tmem_st16(tS + 80, pk);
   tmem_wait_ld_regs(a);
   chunk_exp<6, 16, BF16>(a, c2, b, pk);  // keys 192..207 (196.. get p = 0)
+  uint32_t p8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) p8[e] = pk[e];
+  tmem_st8(tS + 96, p8);
+}
+
+// Exponents x = S*c + rh + rw of the keys of chunk CH below kN (b.rwp may already hold rw minus a
+// reference) into x; returns their max.
+template <int CH>
+__device__ __forceinline__ float chunk_x(const uint32_t (&sv)[32], float2 c2, const Bias& b, float (&x)[32]) {
+  constexpr int NV = (32 * CH + 32 <= kN) ? 32 : (kN - 32 * CH);
+  float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int e = 0; e < NV; e += 2) {
+    const int k0 = 32 * CH + e;
+    const float2 s2 = make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+    const float2 t = sm100::add2(sm100::fma2(s2, c2, b.rhp[k0 / kSide]), b.rwp[(k0 % kSide) >> 1]);
+    x[e] = t.x;
+    x[e + 1] = t.y;
+    mx[(e >> 1) & 3] = sm100::max3(mx[(e >> 1) & 3], t.x, t.y);
+  }
+  return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+}
+
+// 2^x of the chunk's keys below kN (one pair in eight on the FMA pipe) packed as 16-bit pairs; keys >= kN
+// get p = 0.
+template <int CH, int NE, bool BF16>
+__device__ __forceinline__ void chunk_pack(float (&x)[32], uint32_t (&pk)[16]) {
+  constexpr int NV = (32 * CH + NE <= kN) ? NE : (kN - 32 * CH);
+#pragma unroll
+  for (int e = 0; e < NV; e += 2) {
+    if ((e & 14) == 14) {
+      const float2 p = sm100::ex2_poly2(make_float2(x[e], x[e + 1]));
+      x[e] = p.x;
+      x[e + 1] = p.y;
+    } else {
+      x[e] = sm100::ex2(x[e]);
+      x[e + 1] = sm100::ex2(x[e + 1]);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < NE; e += 2) pk[e >> 1] = e < NV ? sm100::pack2(x[e], x[e + 1], BF16) : 0u;
+}
+
+// A later chunk's exponents exceed the row's reference by more than the single pass allows: the reference
+// of every row with such a chunk moves up by d (the chunk's max), so the P already written (columns
+// 0 .. 16 * nprev) are scaled by 2^-d here, and the caller takes d off the chunk's exponents and off the bias
+// pairs of the chunks still to come. The other rows of the warp pass d = 0 (scale by 1). Rare: the overflow
+// guard of the single pass.
+template <bool BF16>
+__device__ __forceinline__ void scale_written_p(uint32_t tS, int nprev, float d) {
+  using namespace sm100;
+  const float f = ex2(-d);
+  tmem_wait_st();  // this thread's P stores are complete before they are read back
+  for (int cc = 0; cc < nprev; ++cc) {
+    uint32_t p[16];
+    tmem_ld16(tS + 16 * cc, p);
+    tmem_wait_ld_regs(p);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      float lo, hi;
+      if (BF16) {
+        lo = __uint_as_float(p[e] << 16);
+        hi = __uint_as_float(p[e] & 0xFFFF0000u);
+      } else {
+        const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(&p[e]));
+        lo = v2.x;
+        hi = v2.y;
+      }
+      p[e] = pack2(lo * f, hi * f, BF16);
+    }
+    tmem_st16(tS + 16 * cc, p);
+  }
+}
+// The same, as a call: at hd 64 the softmax loop measured 18 % faster with the rare path out of line
+// (0.183 vs 0.211 ms at bh 6400), at hd 80 6 % slower than inline (0.430 vs 0.409 ms at bh 12800).
+template <bool BF16>
+__device__ __noinline__ void scale_written_p_call(uint32_t tS, int nprev, float d) {
+  scale_written_p<BF16>(tS, nprev, d);
+}
+
+// Single-pass P for bf16: the reference is the max of the row's first 32 exponents (at or below the row's
+// true max, so the row's largest P is >= 1 and nothing that matters underflows). Later keys' P may exceed 1:
+// bf16 P and the f32 row sums and O hold up to 2^127, and a chunk whose max exceeds the reference by more
+// than kOnlineLimit raises the reference first (scale_written_p), so every P stays <= 2^64. The row sums
+// come from the P.V MMA (ones block of V), from the same rounded P, so any reference gives the same softmax.
+constexpr float kOnlineLimit = 64.f;
+
+template <int CH, int NE, bool BF16, bool OOL>
+__device__ __forceinline__ void online_chunk(const uint32_t (&sv)[32], uint32_t tS, float2 c2, Bias& b,
+                                             uint32_t (&pk)[16]) {
+  float x[32];
+  const float mc = chunk_x<CH>(sv, c2, b, x);
+  if (__any_sync(0xffffffffu, mc > kOnlineLimit)) {
+    const float d = mc > kOnlineLimit ? mc : 0.f;
+    if constexpr (OOL)
+      scale_written_p_call<BF16>(tS, CH, d);
+    else
+      scale_written_p<BF16>(tS, CH, d);
+#pragma unroll
+    for (int k = 0; k < 7; ++k) b.rwp[k] = make_float2(b.rwp[k].x - d, b.rwp[k].y - d);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) x[e] -= d;
+  }
+  chunk_pack<CH, NE, BF16>(x, pk);
+}
+
+template <bool BF16, bool OOL>
+__device__ __forceinline__ void row_exp_online(uint32_t tS, float2 c2, Bias& b) {
+  using namespace sm100;
+  uint32_t a[32], bb[32], pk[16];
+  tmem_ld32(tS + 0, a);
+  tmem_wait_ld_regs(a);
+  tmem_ld32(tS + 32, bb);
+  {
+    float x[32];
+    const float m = chunk_x<0>(a, c2, b, x);
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+      const float2 t = add2(make_float2(x[e], x[e + 1]), make_float2(-m, -m));
+      x[e] = t.x;
+      x[e + 1] = t.y;
+    }
+#pragma unroll
+    for (int k = 0; k < 7; ++k) b.rwp[k] = add2(b.rwp[k], make_float2(-m, -m));
+    chunk_pack<0, 32, BF16>(x, pk);
+  }
+  tmem_st16(tS + 0, pk);
+  tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 64, a);
+  online_chunk<1, 32, BF16, OOL>(bb, tS, c2, b, pk);
+  tmem_st16(tS + 16, pk);
+  tmem_wait_ld_regs(a);
+  tmem_ld32(tS + 96, bb);
+  online_chunk<2, 32, BF16, OOL>(a, tS, c2, b, pk);
+  tmem_st16(tS + 32, pk);
+  tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 128, a);
+  online_chunk<3, 32, BF16, OOL>(bb, tS, c2, b, pk);
+  tmem_st16(tS + 48, pk);
+  tmem_wait_ld_regs(a);
+  tmem_ld32(tS + 160, bb);
+  online_chunk<4, 32, BF16, OOL>(a, tS, c2, b, pk);
+  tmem_st16(tS + 64, pk);
+  tmem_wait_ld_regs(bb);
+  tmem_ld32(tS + 192, a);
+  online_chunk<5, 32, BF16, OOL>(bb, tS, c2, b, pk);
+  tmem_st16(tS + 80, pk);
+  tmem_wait_ld_regs(a);
+  online_chunk<6, 16, BF16, OOL>(a, tS, c2, b, pk);  // keys 192..207 (196.. get p = 0)
   uint32_t p8[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) p8[e] = pk[e];
@@ -486,31 +594,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         Bias b;
         read_bias(tS, i, j, b);
         const float2 c2 = make_float2(c, c);
-        float m;
-        bool exact = !kBf16 || !(c > 0.f);
-        float rhm = -INFINITY, rwm = -INFINITY, rhn = INFINITY, rwn = INFINITY;
-        if (!exact) {
+        if constexpr (kBf16) {
+          row_exp_online<kBf16, HD == 64>(tS, c2, b);
+        } else {
+          // f16 P holds only 2^-14 .. 2^15: the exact max first
+          const float m = row_max(tS, c2, b);
 #pragma unroll
-          for (int k = 0; k < 14; ++k) {
-            rhm = fmaxf(rhm, b.rhp[k].x);
-            rhn = fminf(rhn, b.rhp[k].x);
-          }
-#pragma unroll
-          for (int k = 0; k < 7; ++k) {
-            rwm = max3(rwm, b.rwp[k].x, b.rwp[k].y);
-            rwn = fminf(rwn, fminf(b.rwp[k].x, b.rwp[k].y));
-          }
-          // the bound is at most the rh and rw spreads above the max; keep P of the largest scores
-          // (>= 2^-96) far from the bottom of bf16's range (the whole warp takes the exact pass otherwise)
-          exact = __any_sync(0xffffffffu, (rhm - rhn) + (rwm - rwn) > 96.f);
+          for (int k = 0; k < 7; ++k) b.rwp[k] = make_float2(b.rwp[k].x - m, b.rwp[k].y - m);
+          row_exp<kBf16>(tS, c2, b);
         }
-        if (exact)
-          m = row_max(tS, c2, b);
-        else
-          m = row_max_bound(tS, c, rhm, rwm);
-#pragma unroll
-        for (int k = 0; k < 7; ++k) b.rwp[k] = make_float2(b.rwp[k].x - m, b.rwp[k].y - m);
-        row_exp<kBf16>(tS, c2, b);
         tmem_wait_st();
       }
       tc_fence_before();

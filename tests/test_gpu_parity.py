@@ -181,14 +181,35 @@ def test_window_f32_late_max(samrs, cuda, hd):
 
 @pytest.mark.parametrize("table_std", [0.1, 0.5, 8.0])
 @pytest.mark.parametrize("hd", [64, 80])
-def test_window_bf16_row_max_bound(samrs, cuda, hd, table_std):
-    """bf16 windowed layers take the row max as c * max S + max rh + max rw (above the true max by the
-    row's bias spreads) unless a row's spreads exceed 96 log2 units, when the warp takes the exact max:
-    small tables (bound), the bench's N(0, 0.5) (bound), N(0, 8) (exact). A few keys with large scores
-    make rows dominated by one key."""
+def test_window_bf16_single_pass(samrs, cuda, hd, table_std):
+    """bf16 windowed layers take a single pass per row with the reference from the row's first 32 keys:
+    small tables, the bench's N(0, 0.5), and N(0, 8), whose rh spreads of hundreds of log2 units make later
+    key rows exceed the reference by more than 64 (the reference is raised, the P already written scaled).
+    A few keys with large scores make rows dominated by one key."""
     h = w = 14
     q, kt, v, t = make_inputs(h, w, 40, hd, seed=hd + int(table_std * 10), table_std=table_std)
     kt[::3, :, 17] *= 6.0
+    err = parity_err(*_run_window_bf16(samrs, cuda, q, kt, v, t, hd), "bf16")
+    assert err < HALF_TOL, err
+
+
+@pytest.mark.parametrize("hd", [64, 80])
+def test_window_bf16_late_max_raises_reference(samrs, cuda, hd):
+    """bf16 windowed layers: row maxima that jump past the single pass's reference (the max of the row's first
+    32 keys) by more than 64 log2 units in a later 32-key chunk, once (chunk 1), twice (chunks 1 and 4), three
+    times (chunks 1, 4 and the last, partly masked chunk 6) or only in the last chunk; heads whose jump stays
+    below the limit (P up to 2^39, no raise) and heads without a jump. Only the even query rows see the jumps,
+    so every warp mixes rows that raise the reference with rows that keep it."""
+    h = w = 14
+    bh = 24
+    q, kt, v, t = make_inputs(h, w, bh, hd, seed=hd + 11, table_std=0.5)
+    q[:, ::2, 0] = 4.0
+    for b in range(bh):
+        kind = b % 6
+        keys = {0: [], 1: [40], 2: [40, 150], 3: [40, 150, 195], 4: [195], 5: [100]}[kind]
+        bigs = {4: [120.0], 5: [60.0]}.get(kind, [120.0, 250.0, 400.0])
+        for key, big in zip(keys, bigs):
+            kt[b, 0, key] = big
     err = parity_err(*_run_window_bf16(samrs, cuda, q, kt, v, t, hd), "bf16")
     assert err < HALF_TOL, err
 
