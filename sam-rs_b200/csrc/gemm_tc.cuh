@@ -10,18 +10,23 @@
 //                     window-partitioned grid, src/sam1/encoder.rs:132-140; the pad tokens are written by
 //                     qkv_pad_fill_kernel, see window_io.cuh)
 //
-// Structure: persistent grid (one CTA per SM) over 128 x 256 output tiles, rows of A fastest-varying tiles
-// sharing them back to back (the A tile stays in L2 across the N tiles of its row). 12 or 20 warps:
-//   warp 0   TMA producer: A [128 x 64] and W [256 x 64] boxes (128-byte swizzle) into a 4-stage ring
-//   warp 1   MMA issuer (the warp runs the loop, lane 0 issues): 4 x tcgen05.mma M=128 N=256 K=16 per stage
+// Structure: persistent grid over output tiles, rows of A fastest-varying tiles sharing them back to back
+// (the A tile stays in L2 across the N tiles of its row). By default a tile is 256 x 256 and belongs to a
+// CTA pair (a cluster of two CTAs on two SMs, one cta_group::2 MMA of M = 256): each CTA loads its 128 rows of
+// A and its 128 rows of W, so a pair reads W once per 256 rows instead of once per 128, and each SM stages
+// 32 KB per k-step instead of 48 KB (6 stages in flight instead of 4). Where no 2-CTA cluster can be resident
+// the same kernel runs one CTA per 128 x 256 tile. Warps:
+//   warp 0   TMA producer: A [128 x 64] and W [128 x 64] (pair) or [256 x 64] boxes, 128-byte swizzle. A pair's
+//            loads all complete on the leader's (rank 0's) full barrier.
+//   warp 1   MMA issuer, leader only (the warp runs the loop, lane 0 issues): 4 x tcgen05.mma K=16 per stage,
+//            N = 256, M = 256 (pair) or 128; commits go to the barriers of both CTAs of a pair.
 //   warp 2   TMEM allocator (512 columns: two 256-column accumulators, so the epilogue of one tile overlaps
-//            the main loop of the next)
-//   warps 4+ epilogue (epi_warps: 8, or 16 for the GELU): two or four warps per TMEM lane quarter, each
-//            taking a slice of the tile's columns; thread = output row (TMEM lane), 16-column groups read with
-//            tcgen05.ld, the epilogue applied in f32, 16-byte stores of the row's columns. Several warps per
-//            quarter keep the epilogue (erf of the GELU, the k^T scatter of the qkv layout) shorter than the
-//            main loop of a tile.
-// No multicast anywhere; every wait is bounded (sm100::mbar_wait).
+//            the main loop of the next; a pair allocates with cta_group::2 in both CTAs)
+//   warps 4+ epilogue (epi_warps: 16 in the pair kernel and for the GELU, else 8): warps per TMEM lane quarter
+//            each take a slice of the tile's columns; thread = output row (TMEM lane), 16-column groups read
+//            with tcgen05.ld, the epilogue applied in f32, 16-byte stores of the row's columns. A pair's
+//            epilogue warps hand the accumulator back on the leader's acc_empty barrier.
+// No multicast anywhere; every wait on an mbarrier is bounded (sm100::mbar_wait).
 #pragma once
 #include <cuda.h>
 
@@ -33,20 +38,28 @@
 namespace samrs {
 namespace tgemm {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
-constexpr int kABytes = kBM * kBK * 2;  // 16 KB
-constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
-static_assert(kSmemBytes <= 232448, "shared memory budget");
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kABytes = kBM * kBK * 2;  // 16 KB: this CTA's 128 rows of A per stage
+// Stage layout. One CTA: A [128 x 64] and W [256 x 64] (48 KB), 4 stages. CTA pair (cta_group::2, a 256 x 256
+// tile per pair): each CTA holds its 128 rows of A and its 128 rows of W (32 KB), 6 stages.
+__host__ __device__ constexpr int b_rows(bool pair) { return pair ? kBN / 2 : kBN; }
+__host__ __device__ constexpr int stage_bytes(bool pair) { return kABytes + b_rows(pair) * kBK * 2; }
+__host__ __device__ constexpr int stages(bool pair) { return pair ? 6 : 4; }
+__host__ __device__ constexpr int smem_bytes(bool pair) { return stages(pair) * stage_bytes(pair) + 256 + 1024; }
+__host__ __device__ constexpr int tile_m(bool pair) { return pair ? 2 * kBM : kBM; }
+constexpr int kMaxStages = 6;
+static_assert(smem_bytes(false) <= 232448 && smem_bytes(true) <= 232448, "shared memory budget");
 
 enum Epi : int { kEpiBias = 0, kEpiBiasResidual = 1, kEpiBiasGelu = 2, kEpiQkvWindow = 3 };
 
 // Epilogue warps per CTA: 16 (four per TMEM lane quarter) for the erf GELU, whose per-tile epilogue at
-// K = 768 issues more instructions than the tile's main loop and needs the extra warps to hide latency;
-// 8 for the others, where more warps only add contention for the store path.
-__host__ __device__ constexpr int epi_warps(int epi) { return epi == kEpiBiasGelu ? 16 : 8; }
-__host__ __device__ constexpr int threads_for(int epi) { return 128 + 32 * epi_warps(epi); }
+// K = 768 issues more instructions than the tile's main loop and needs the extra warps to hide latency, and
+// for every epilogue of the CTA-pair kernel, whose main loop per tile is shorter (ViT-H qkv 1.34 -> 1.24 ms,
+// lin2 1.46 -> 1.41 ms with 16 instead of 8); 8 for the others in the single-CTA kernel.
+__host__ __device__ constexpr int epi_warps(int epi, bool pair = false) {
+  return (epi == kEpiBiasGelu || pair) ? 16 : 8;
+}
+__host__ __device__ constexpr int threads_for(int epi, bool pair = false) { return 128 + 32 * epi_warps(epi, pair); }
 
 // Window geometry of the qkv epilogue: token m = (image, y, x) of an H x W grid cut into ws x ws windows
 // (ws = 0: the whole grid is one window), windows row-major per image over the grid padded up to multiples
@@ -60,6 +73,7 @@ struct QkvGeom {
 struct Params {
   int M, N, K;
   int group;  // M blocks whose tiles of one N block run side by side (1: the tiles of an M block run together)
+  int band_rows;  // rows of A that one group should cover (0: group = 1); the launch sets `group` from it
   const void* bias;  // [N]
   const void* res;   // [M, N] (kEpiBiasResidual)
   void* out;         // [M, N], or the packed q | kt | v planes (kEpiQkvWindow)
@@ -67,11 +81,12 @@ struct Params {
 };
 
 struct Bars {
-  uint64_t full[kStages], empty[kStages];
+  uint64_t full[kMaxStages], empty[kMaxStages];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t final_mma;
   uint32_t tmem_base;
   int abort_flag;
+  int skip;  // CTA pair: rank 0's decision to leave at entry (a fault reported earlier), read by both CTAs
 };
 
 template <typename T>
@@ -190,28 +205,38 @@ __device__ __forceinline__ void epilogue16(const Params& p, bool row_ok, int m, 
 // the group's M blocks of one N block are computed at the same time (the qkv epilogue's band of window rows:
 // each k^T row of a window is then written whole within one wave), and with p.group = 1 the N blocks of one
 // M block run back to back (its A tile stays in L2).
-__device__ __forceinline__ void tile_coords(const Params& p, int m_blocks, int n_blocks, int t, int& m0, int& n0) {
+__device__ __forceinline__ void tile_coords(const Params& p, int m_blocks, int n_blocks, int t, int& m0, int& n0,
+                                            int bm = kBM) {
   const int gsize = p.group * n_blocks;
   const int grp = t / gsize, r = t - grp * gsize;
   const int gm = m_blocks - grp * p.group < p.group ? m_blocks - grp * p.group : p.group;  // M blocks in the group
   const int nb = r / gm, mb = grp * p.group + (r - nb * gm);
-  m0 = mb * kBM;
+  m0 = mb * bm;
   n0 = nb * kBN;
 }
 
-template <typename T, int EPI>
-__global__ void __launch_bounds__(threads_for(EPI), 1)
+template <typename T, int EPI, bool kPair>
+__global__ void __launch_bounds__(threads_for(EPI, kPair), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
   using namespace sm100;
-  constexpr int kEpiWarps = epi_warps(EPI);
+  constexpr int kEpiWarps = epi_warps(EPI, kPair);
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int kStages = stages(kPair), kStageBytes = stage_bytes(kPair), kTM = tile_m(kPair);
   extern __shared__ uint8_t smem_raw[];
-  if (__syncthreads_or(threadIdx.x == 0 && device_faulted())) return;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kStages * kStageBytes);
   volatile int* abort_flag = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_blocks = (p.M + kBM - 1) / kBM, n_blocks = (p.N + kBN - 1) / kBN;
+  // CTA pair: rank 0 (the leader) issues the pair's MMAs and owns the full and acc_empty barriers; both CTAs
+  // load their halves of A and W, and run the epilogue of their 128 rows.
+  const uint32_t rank = kPair ? cluster_rank() : 0;
+  const bool leader = rank == 0;
+  const int unit = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // the pair (or CTA) index
+  const int n_units = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  if constexpr (!kPair) {
+    if (__syncthreads_or(threadIdx.x == 0 && device_faulted())) return;
+  }
+  const int m_blocks = (p.M + kTM - 1) / kTM, n_blocks = (p.N + kBN - 1) / kBN;
   const int tiles = m_blocks * n_blocks;
   const int nk = (p.K + kBK - 1) / kBK;
 
@@ -222,19 +247,36 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&bars->acc_full[a], 1);
-      mbar_init(&bars->acc_empty[a], kEpiWarps);  // one arrival per epilogue warp
+      mbar_init(&bars->acc_empty[a], kPair ? 2 * kEpiWarps : kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(&bars->final_mma, 1);
     bars->abort_flag = 0;
+    bars->skip = kPair && leader ? (int)device_faulted() : 0;
     fence_mbar_init();
   }
-  if (warp == 2) {
-    tmem_alloc(&bars->tmem_base, 512);
-    tmem_relinquish();
+  if constexpr (kPair) {
+    // Both CTAs leave together after an earlier CTA reported a fault (rank 0 decides; the second cluster
+    // barrier keeps rank 0's shared memory alive until rank 1 has read the decision).
+    cluster_sync();
+    const int skip = ld_cluster_s32(cluster_addr(&bars->skip, 0));
+    cluster_sync();
+    if (skip) return;
+    if (warp == 2) {
+      tmem_alloc_pair(&bars->tmem_base, 512);
+      tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers initialised and TMEM allocated in both CTAs before any load or MMA
+    tc_fence_after();
+  } else {
+    if (warp == 2) {
+      tmem_alloc(&bars->tmem_base, 512);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == 0) {
@@ -244,9 +286,9 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
       tma_prefetch_desc(&tmB);
       int it = 0;
       bool okk = true;
-      for (int tile = blockIdx.x; tile < tiles && okk; tile += gridDim.x) {
+      for (int tile = unit; tile < tiles && okk; tile += n_units) {
         int m0, n0;
-        tile_coords(p, m_blocks, n_blocks, tile, m0, n0);
+        tile_coords(p, m_blocks, n_blocks, tile, m0, n0, kTM);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % kStages;
           if (it >= kStages && !mbar_wait(&bars->empty[s], ((it / kStages) - 1) & 1, abort_flag)) {
@@ -254,47 +296,71 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
             break;
           }
           uint8_t* st = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
-          tma_load_2d(st, &tmA, &bars->full[s], kb * kBK, m0);
-          tma_load_2d(st + kABytes, &tmB, &bars->full[s], kb * kBK, n0);
+          if constexpr (kPair) {
+            // both halves' bytes complete on the leader's barrier
+            const uint32_t full = cluster_addr(&bars->full[s], 0);
+            if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kStageBytes);
+            tma_load_2d_pair(st, &tmA, full, kb * kBK, m0 + kBM * (int)rank);
+            tma_load_2d_pair(st + kABytes, &tmB, full, kb * kBK, n0 + (kBN / 2) * (int)rank);
+          } else {
+            mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+            tma_load_2d(st, &tmA, &bars->full[s], kb * kBK, m0);
+            tma_load_2d(st + kABytes, &tmB, &bars->full[s], kb * kBK, n0);
+          }
         }
       }
-      if (*abort_flag) {
-        // drain this CTA's own copies still in flight before the CTA can exit
+      if (*abort_flag && leader) {
+        // drain the copies still in flight before the CTA can exit (a pair's copies all count on the leader)
         for (int j = it > kStages ? it - kStages : 0; j < it; ++j) mbar_drain(&bars->full[j % kStages], (j / kStages) & 1);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = idesc_f16(kBf16, kBM, kBN, false, false);
-    const uint32_t sb = smem_u32(smem);
-    // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart; K steps of 16 advance 32 B
-    const uint64_t dA = smem_desc(sb, 16, 1024, kLayoutSw128);
-    const uint64_t dB = smem_desc(sb + kABytes, 16, 1024, kLayoutSw128);
-    auto wait = [&](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag)); };
-    int it = 0, ti = 0;
-    bool okk = true;
-    for (int tile = blockIdx.x; tile < tiles && okk; tile += gridDim.x, ++ti) {
-      const int ab = ti & 1;
-      // the epilogue has read this accumulator's previous tile
-      if (ti >= 2 && !(okk = wait(&bars->acc_empty[ab], ((ti >> 1) - 1) & 1))) break;
-      tc_fence_after();
-      const uint32_t tacc = tmem + ab * kBN;
-      for (int kb = 0; kb < nk; ++kb, ++it) {
-        const int s = it % kStages;
-        if (!(okk = wait(&bars->full[s], (it / kStages) & 1))) break;
+    if (leader) {
+      constexpr uint32_t idesc = idesc_f16(kBf16, kTM, kBN, false, false);
+      const uint32_t sb = smem_u32(smem);
+      // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart; K steps of 16 advance 32 B
+      const uint64_t dA = smem_desc(sb, 16, 1024, kLayoutSw128);
+      const uint64_t dB = smem_desc(sb + kABytes, 16, 1024, kLayoutSw128);
+      auto wait = [&](uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag)); };
+      // commit to a barrier of this CTA, and for a pair to the same barrier of the other CTA as well
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (kPair) {
+          mma_commit_pair_w(cluster_addr(bar, 0));
+          mma_commit_pair_w(cluster_addr(bar, 1));
+        } else {
+          mma_commit_w(bar);
+        }
+      };
+      int it = 0, ti = 0;
+      bool okk = true;
+      for (int tile = unit; tile < tiles && okk; tile += n_units, ++ti) {
+        const int ab = ti & 1;
+        // the epilogue (of both CTAs) has read this accumulator's previous tile
+        if (ti >= 2 && !(okk = wait(&bars->acc_empty[ab], ((ti >> 1) - 1) & 1))) break;
         tc_fence_after();
+        const uint32_t tacc = tmem + ab * kBN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!(okk = wait(&bars->full[s], (it / kStages) & 1))) break;
+          tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)
-          mma_ss_w(tacc, desc_add(dA, s * kStageBytes + 32 * k), desc_add(dB, s * kStageBytes + 32 * k), idesc,
-                   (kb > 0 || k > 0) ? 1u : 0u);
-        mma_commit_w(&bars->empty[s]);  // the stage may be refilled once these MMAs completed
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t a = desc_add(dA, s * kStageBytes + 32 * k), bd = desc_add(dB, s * kStageBytes + 32 * k);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            if constexpr (kPair)
+              mma_ss_pair_w(tacc, a, bd, idesc, acc);
+            else
+              mma_ss_w(tacc, a, bd, idesc, acc);
+          }
+          commit(&bars->empty[s]);  // the stage may be refilled once these MMAs completed
+        }
+        if (!okk) break;
+        commit(&bars->acc_full[ab]);
       }
-      if (!okk) break;
-      mma_commit_w(&bars->acc_full[ab]);
+      // every MMA issued by this warp has completed before the CTA (pair) tears down TMEM
+      commit(&bars->final_mma);
     }
-    // every MMA issued by this warp has completed before the CTA tears down TMEM
-    mma_commit_w(&bars->final_mma);
     mbar_drain(&bars->final_mma, 0);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
@@ -302,11 +368,11 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     const int half = (warp - 4) >> 2;  // column slice of the tile (kEpiWarps / 4 slices)
     constexpr int kGroups = kBN / 16 / (kEpiWarps / 4);
     int ti = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
+    for (int tile = unit; tile < tiles; tile += n_units, ++ti) {
       const int ab = ti & 1;
       int m0, n0;
-      tile_coords(p, m_blocks, n_blocks, tile, m0, n0);
-      const int m = m0 + 32 * wq + lane;
+      tile_coords(p, m_blocks, n_blocks, tile, m0, n0, kTM);
+      const int m = m0 + kBM * (int)rank + 32 * wq + lane;
       const bool row_ok = m < p.M;
       // the residual's columns of this thread, loaded while the tile's main loop still runs
       constexpr int kRes = EPI == kEpiBiasResidual ? kGroups : 1;
@@ -351,7 +417,12 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
           // every column of this accumulator is in registers: hand it back to the MMA warp
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->acc_empty[ab]);
+          if (lane == 0) {
+            if constexpr (kPair)
+              mbar_arrive_cluster(cluster_addr(&bars->acc_empty[ab], 0));
+            else
+              mbar_arrive(&bars->acc_empty[ab]);
+          }
         }
         const int n = n0 + 16 * (kGroups * half + grp);
         if (n < p.N) {  // warp-uniform (the qkv epilogue's lane pairs exchange values: every lane takes part)
@@ -364,10 +435,19 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     }
   }
   tc_fence_before();
-  __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
+  if constexpr (kPair) {
+    // neither CTA leaves while the pair's MMAs, copies or arrivals may still touch the other's memory
+    cluster_sync();
+    if (warp == 2) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem, 512);
+    }
+  } else {
+    __syncthreads();
+    if (warp == 2) {
+      tc_fence_after();
+      tmem_dealloc(tmem, 512);
+    }
   }
 }
 

@@ -238,20 +238,82 @@ int launch_merge(const void* attn, void* out, int64_t images, const WinGeom& g, 
 }
 
 // ---------------------------------------------------------------------------------------- GEMM
-template <typename T, int EPI>
-int launch_gemm(const void* a, const void* w, const tgemm::Params& p, cudaStream_t st, int num_sms) {
+// A CTA pair (cluster of 2, one cta_group::2 MMA) per 256 x 256 tile; one CTA per 128 x 256 tile where
+// no 2-CTA cluster can be resident (a device partition that does not offer clusters).
+template <typename T, int EPI, bool kPair>
+int launch_gemm_as(const void* a, const void* w, tgemm::Params p, cudaStream_t st, int num_sms, int clusters) {
   constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int tm = tgemm::tile_m(kPair), smem = tgemm::smem_bytes(kPair);
+  p.group = p.band_rows > 0 ? std::max(1, std::min(16, (p.band_rows + tm - 1) / tm)) : 1;
   CUtensorMap ma, mb;
   int rc = tcg::make_map(&ma, bf16, a, (uint64_t)p.K, (uint64_t)p.M, tgemm::kBK, tgemm::kBM, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = tcg::make_map(&mb, bf16, w, (uint64_t)p.K, (uint64_t)p.N, tgemm::kBK, tgemm::kBN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = tcg::make_map(&mb, bf16, w, (uint64_t)p.K, (uint64_t)p.N, tgemm::kBK, tgemm::b_rows(kPair),
+                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return fail(SAMRS_ERR_LAUNCH, "linear: %s", tc_error_string(rc));
-  auto kern = tgemm::gemm_kernel<T, EPI>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tgemm::kSmemBytes) != cudaSuccess)
-    return fail(SAMRS_ERR_LAUNCH, "linear: cannot set the kernel's shared memory size");
-  const long tiles = (long)((p.M + tgemm::kBM - 1) / tgemm::kBM) * ((p.N + tgemm::kBN - 1) / tgemm::kBN);
-  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
-  kern<<<grid, tgemm::threads_for(EPI), tgemm::kSmemBytes, st>>>(ma, mb, p);
-  return launch_status("linear");
+  auto kern = tgemm::gemm_kernel<T, EPI, kPair>;
+  const long tiles = (long)((p.M + tm - 1) / tm) * ((p.N + tgemm::kBN - 1) / tgemm::kBN);
+  if (!kPair) {
+    const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+    kern<<<grid, tgemm::threads_for(EPI, false), smem, st>>>(ma, mb, p);
+    return launch_status("linear");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(tgemm::threads_for(EPI, true));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // a persistent grid: as many pairs as are resident at once, at most one per tile
+  cfg.gridDim = dim3(2 * (unsigned)(tiles < clusters ? tiles : clusters));
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, p);
+  if (e != cudaSuccess) return fail(SAMRS_ERR_LAUNCH, "linear (CTA pairs): launch failed: %s", cudaGetErrorString(e));
+  return launch_status("linear (CTA pairs)");
+}
+
+// 2-CTA clusters of this kernel that can be resident at once on the current device (0: none), once per
+// device and kernel.
+template <typename T, int EPI>
+int pair_clusters(int dev, int num_sms) {
+  static std::once_flag once[kMaxDevices];
+  static int clusters[kMaxDevices];
+  std::call_once(once[dev], [&]() {
+    auto kern = tgemm::gemm_kernel<T, EPI, true>;
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tgemm::smem_bytes(true)) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (unsigned)(num_sms / 2));
+      cfg.blockDim = dim3(tgemm::threads_for(EPI, true));
+      cfg.dynamicSmemBytes = tgemm::smem_bytes(true);
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaFuncSetAttribute(tgemm::gemm_kernel<T, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         tgemm::smem_bytes(false));
+    cudaGetLastError();  // a refused query leaves no sticky error behind
+    clusters[dev] = n;
+  });
+  return clusters[dev];
+}
+
+template <typename T, int EPI>
+int launch_gemm(const void* a, const void* w, const tgemm::Params& p, cudaStream_t st, int num_sms) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int clusters = pair_clusters<T, EPI>(dev, num_sms);
+  return clusters > 0 ? launch_gemm_as<T, EPI, true>(a, w, p, st, num_sms, clusters)
+                      : launch_gemm_as<T, EPI, false>(a, w, p, st, num_sms, 0);
 }
 
 template <typename T>
@@ -525,7 +587,7 @@ int samrs_qkv_linear_window_fwd(const void* x, const void* w, const void* bias, 
   p.N = 3 * c;
   p.K = c;
   // the M blocks of one band of window rows (ws grid rows of every image column) run side by side
-  p.group = ws ? (int)std::max<int64_t>(1, std::min<int64_t>(16, ((int64_t)g.wh * w_grid + tgemm::kBM - 1) / tgemm::kBM)) : 1;
+  p.band_rows = ws ? (int)std::min<int64_t>((int64_t)g.wh * w_grid, 1 << 20) : 0;
   p.bias = bias;
   p.out = out;
   const int pairs = w_grid % 2 == 0 && g.ww % 2 == 0;  // ws = 0: g.ww = w_grid
