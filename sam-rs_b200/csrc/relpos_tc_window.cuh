@@ -258,14 +258,16 @@ __device__ __forceinline__ float chunk_x(const uint32_t (&sv)[32], float2 c2, co
   return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
 }
 
-// 2^x of the chunk's keys below kN (one pair in eight on the FMA pipe) packed as 16-bit pairs; keys >= kN
-// get p = 0.
-template <int CH, int NE, bool BF16>
+// 2^x of the chunk's keys below kN packed as 16-bit pairs; keys >= kN get p = 0. With POLY, one key pair in
+// eight goes to the FMA-pipe polynomial: at hd 80 that measured 0.389 ms against 0.405 (one in four), 0.406
+// (one in sixteen) and 0.413 (none) per bh-12800 layer; at hd 64 none measured best (0.178 against 0.181 with
+// one in eight, bh 6400).
+template <int CH, int NE, bool BF16, bool POLY>
 __device__ __forceinline__ void chunk_pack(float (&x)[32], uint32_t (&pk)[16]) {
   constexpr int NV = (32 * CH + NE <= kN) ? NE : (kN - 32 * CH);
 #pragma unroll
   for (int e = 0; e < NV; e += 2) {
-    if ((e & 14) == 14) {
+    if (POLY && (e & 14) == 14) {
       const float2 p = sm100::ex2_poly2(make_float2(x[e], x[e + 1]));
       x[e] = p.x;
       x[e + 1] = p.y;
@@ -322,7 +324,7 @@ __device__ __noinline__ void scale_written_p_call(uint32_t tS, int nprev, float 
 // come from the P.V MMA (ones block of V), from the same rounded P, so any reference gives the same softmax.
 constexpr float kOnlineLimit = 64.f;
 
-template <int CH, int NE, bool BF16, bool OOL>
+template <int CH, int NE, bool BF16, int HD, bool OOL>
 __device__ __forceinline__ void online_chunk(const uint32_t (&sv)[32], uint32_t tS, float2 c2, Bias& b,
                                              uint32_t (&pk)[16]) {
   float x[32];
@@ -338,10 +340,10 @@ __device__ __forceinline__ void online_chunk(const uint32_t (&sv)[32], uint32_t 
 #pragma unroll
     for (int e = 0; e < 32; ++e) x[e] -= d;
   }
-  chunk_pack<CH, NE, BF16>(x, pk);
+  chunk_pack<CH, NE, BF16, HD != 64>(x, pk);
 }
 
-template <bool BF16, bool OOL>
+template <bool BF16, int HD, bool OOL>
 __device__ __forceinline__ void row_exp_online(uint32_t tS, float2 c2, Bias& b) {
   using namespace sm100;
   uint32_t a[32], bb[32], pk[16];
@@ -359,31 +361,31 @@ __device__ __forceinline__ void row_exp_online(uint32_t tS, float2 c2, Bias& b) 
     }
 #pragma unroll
     for (int k = 0; k < 7; ++k) b.rwp[k] = add2(b.rwp[k], make_float2(-m, -m));
-    chunk_pack<0, 32, BF16>(x, pk);
+    chunk_pack<0, 32, BF16, HD != 64>(x, pk);
   }
   tmem_st16(tS + 0, pk);
   tmem_wait_ld_regs(bb);
   tmem_ld32(tS + 64, a);
-  online_chunk<1, 32, BF16, OOL>(bb, tS, c2, b, pk);
+  online_chunk<1, 32, BF16, HD, OOL>(bb, tS, c2, b, pk);
   tmem_st16(tS + 16, pk);
   tmem_wait_ld_regs(a);
   tmem_ld32(tS + 96, bb);
-  online_chunk<2, 32, BF16, OOL>(a, tS, c2, b, pk);
+  online_chunk<2, 32, BF16, HD, OOL>(a, tS, c2, b, pk);
   tmem_st16(tS + 32, pk);
   tmem_wait_ld_regs(bb);
   tmem_ld32(tS + 128, a);
-  online_chunk<3, 32, BF16, OOL>(bb, tS, c2, b, pk);
+  online_chunk<3, 32, BF16, HD, OOL>(bb, tS, c2, b, pk);
   tmem_st16(tS + 48, pk);
   tmem_wait_ld_regs(a);
   tmem_ld32(tS + 160, bb);
-  online_chunk<4, 32, BF16, OOL>(a, tS, c2, b, pk);
+  online_chunk<4, 32, BF16, HD, OOL>(a, tS, c2, b, pk);
   tmem_st16(tS + 64, pk);
   tmem_wait_ld_regs(bb);
   tmem_ld32(tS + 192, a);
-  online_chunk<5, 32, BF16, OOL>(bb, tS, c2, b, pk);
+  online_chunk<5, 32, BF16, HD, OOL>(bb, tS, c2, b, pk);
   tmem_st16(tS + 80, pk);
   tmem_wait_ld_regs(a);
-  online_chunk<6, 16, BF16, OOL>(a, tS, c2, b, pk);  // keys 192..207 (196.. get p = 0)
+  online_chunk<6, 16, BF16, HD, OOL>(a, tS, c2, b, pk);  // keys 192..207 (196.. get p = 0)
   uint32_t p8[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) p8[e] = pk[e];
@@ -595,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         read_bias(tS, i, j, b);
         const float2 c2 = make_float2(c, c);
         if constexpr (kBf16) {
-          row_exp_online<kBf16, HD == 64>(tS, c2, b);
+          row_exp_online<kBf16, HD, HD == 64>(tS, c2, b);
         } else {
           // f16 P holds only 2^-14 .. 2^15: the exact max first
           const float m = row_max(tS, c2, b);

@@ -9,6 +9,7 @@
 #include <mutex>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "../../include/samrs_b200.h"
 #include "common.cuh"
@@ -277,7 +278,8 @@ int launch_gemm_as(const void* a, const void* w, tgemm::Params p, cudaStream_t s
 }
 
 // 2-CTA clusters of this kernel that can be resident at once on the current device (0: none), once per
-// device and kernel.
+// device and kernel. SAMRS_GEMM_SINGLE_CTA=1 in the environment forces the single-CTA kernel (0 clusters),
+// which is how the tests compare the two.
 template <typename T, int EPI>
 int pair_clusters(int dev, int num_sms) {
   static std::once_flag once[kMaxDevices];
@@ -299,6 +301,8 @@ int pair_clusters(int dev, int num_sms) {
       cfg.numAttrs = 1;
       if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
     }
+    const char* force_single = getenv("SAMRS_GEMM_SINGLE_CTA");
+    if (force_single && force_single[0] == '1') n = 0;
     cudaFuncSetAttribute(tgemm::gemm_kernel<T, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          tgemm::smem_bytes(false));
     cudaGetLastError();  // a refused query leaves no sticky error behind

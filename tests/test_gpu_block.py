@@ -2,6 +2,10 @@
 the reference (src/sam1/encoder.rs:89-129): the tensor-core Linear with its three fused epilogues, the qkv
 projection fused with the window partition and head split, LayerNorm, one windowed and one global block, and
 BASELINE config 2's ViT-B stack (12 blocks, f16)."""
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -116,3 +120,48 @@ def test_vitb_stack_config2(samrs, cuda):
     assert samrs.device_status() == 0
     assert rel_max_err(r(y), ref) < 1e-2
     assert mean_rel_err(r(y), ref) < 2e-3
+
+
+_GEMM_CHILD = r"""
+import importlib, sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[2])
+samrs = importlib.import_module("sam-rs_b200")
+dev = torch.device("cuda:0")
+g = torch.Generator(device=dev).manual_seed(11)
+outs = {}
+for dt in (torch.bfloat16, torch.float16):
+    for m, n, k in ((1000, 2304, 768), (257, 1280, 5120), (4096, 3840, 1280), (64, 80, 40)):
+        a = torch.randn(m, k, generator=g, device=dev).to(dt)
+        w = (0.05 * torch.randn(n, k, generator=g, device=dev)).to(dt)
+        b = (0.1 * torch.randn(n, generator=g, device=dev)).to(dt)
+        res = torch.randn(m, n, generator=g, device=dev).to(dt)
+        for epi in ("bias", "bias_residual", "bias_gelu"):
+            y = samrs.linear(a, w, b, res=res if epi == "bias_residual" else None, epilogue=epi)
+            outs[f"{dt}-{m}-{n}-{k}-{epi}"] = y.view(torch.int16).cpu().numpy()
+    x = torch.randn(2 * 64 * 64, 768, generator=g, device=dev).to(dt)
+    wq = (0.05 * torch.randn(3 * 768, 768, generator=g, device=dev)).to(dt)
+    bq = torch.randn(3 * 768, generator=g, device=dev).to(dt)
+    for i, t in enumerate(samrs.qkv_linear_window(x, wq, bq, 2, 64, 64, 14, 12, 64)):
+        outs[f"{dt}-qkv-{i}"] = t.contiguous().view(torch.int16).cpu().numpy()
+assert samrs.device_status() == 0
+np.savez(sys.argv[1], **outs)
+"""
+
+
+def test_single_cta_gemm_matches_cta_pairs(tmp_path):
+    """The single-CTA GEMM kernel (one CTA per 128 x 256 tile, used where no 2-CTA cluster can be resident;
+    forced with SAMRS_GEMM_SINGLE_CTA=1) writes bit for bit what the CTA-pair kernel writes: the three Linear
+    epilogues at ragged and ViT-H shapes (K 40 .. 5120) and the fused qkv window layout, bf16 and f16. Each
+    path runs in a child process of its own, since the choice is made once per process."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    files = {}
+    for single in ("0", "1"):
+        env = dict(os.environ, SAMRS_GEMM_SINGLE_CTA=single)
+        f = str(tmp_path / f"gemm_{single}.npz")
+        subprocess.run([sys.executable, "-c", _GEMM_CHILD, f, root], env=env, check=True, timeout=600)
+        files[single] = np.load(f)
+    assert set(files["0"].files) == set(files["1"].files)
+    for key in files["0"].files:
+        assert np.array_equal(files["0"][key], files["1"][key]), key
