@@ -413,6 +413,30 @@ def bind_to_gpu_numa_node(local_rank):
         return None
 
 
+def relpos_attention_fp32(torch, q, kt, v, table, h, w, scale):
+    """Plain PyTorch fp32 reference of the op on the device (the math of the reference's tensor definition,
+    src/kernels.rs:20-42): softmax(scale q kt + q.Th[i-kh+h-1] + q.Tw[j-kw+w-1]) v with the N x N scores
+    materialised. q, v [b, n, hd]; kt [b, hd, n]; table [(2h-1)+(2w-1), hd]; all fp32."""
+    b, n, hd = q.shape
+    dev = q.device
+    th, tw = table[: 2 * h - 1], table[2 * h - 1:]
+    ih = torch.arange(h, device=dev)
+    iw = torch.arange(w, device=dev)
+    rel_h = th[ih[:, None] - ih[None, :] + h - 1]  # [i, kh, hd]
+    rel_w = tw[iw[:, None] - iw[None, :] + w - 1]  # [j, kw, hd]
+    qg = q.view(b, h, w, hd)
+    rh = torch.einsum("bijd,ikd->bijk", qg, rel_h)  # [b, i, j, kh]
+    rw = torch.einsum("bijd,jkd->bijk", qg, rel_w)  # [b, i, j, kw]
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        s = torch.bmm(q, kt) * scale
+        s = s.view(b, h, w, h, w) + rh[:, :, :, :, None] + rw[:, :, :, None, :]
+        return torch.bmm(torch.softmax(s.view(b, n, n), dim=-1), v)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+
+
 class Step:
     """The layers of one step of a workload, with inputs resident on the device (drawn in a fixed order from a
     per-rank generator, so a rank's inputs and outputs do not depend on the world size)."""
@@ -451,6 +475,20 @@ class Step:
 
     def checksums(self):
         return [float(self.sets[k]["out"].float().sum().item()) for k in KINDS]
+
+    def sampled_parity(self, torch, heads=(2, 8)):
+        """Plain max|got-ref|/max|ref| of heads sampled evenly over the batch (2 global, 8 windowed) of each
+        kind's last output (its last layer's table) against relpos_attention_fp32 on the same bf16 inputs."""
+        errs = []
+        for kind, nh in zip(KINDS, heads):
+            li = max(i for i, g in enumerate(self.geoms) if g[0] == kind)
+            _, h, w, bh = self.geoms[li]
+            st = self.sets[kind]
+            idx = torch.linspace(0, bh - 1, nh, device=st["q"].device).round().long().unique()
+            ref = relpos_attention_fp32(torch, st["q"][idx].float(), st["kt"][idx].float(), st["v"][idx].float(),
+                                        self.tables[li].float(), h, w, self.scale)
+            errs.append(float((st["out"][idx].float() - ref).abs().max() / ref.abs().max()))
+        return errs
 
 
 def time_workload(torch, samrs, step, stream, dist, device, steps, warmup, per_launch=False, clocks=None):
@@ -588,8 +626,8 @@ def run_ours(args):
     status = samrs.device_status()
     summ = summary_line(step, world, K, max_ms)
 
-    # checksums of the last outputs and per-rank status, gathered to rank 0 (after timing)
-    all_csum = gather_floats(step.checksums() + [local_ms, float(status)], dist, device)
+    # checksums of the last outputs, sampled parity, per-rank time and status, gathered to rank 0 (after timing)
+    all_csum = gather_floats(step.checksums() + step.sampled_parity(torch) + [local_ms, float(status)], dist, device)
     traffic = load_traffic() if args.config == 4 else {}
 
     def roof(kind):
@@ -666,6 +704,10 @@ def run_ours(args):
             "device_status": [int(c[-1]) for c in all_csum],
             "rank_ms": [c[-2] for c in all_csum],
             "checksums": [c[:2] for c in all_csum],
+            "parity_vs_torch_fp32": {
+                "what": "plain max|got-ref|/max|ref| per rank of sampled heads (2 global, 8 windowed) of the last "
+                        "outputs against a PyTorch fp32 reference on the same bf16 inputs (bar 3e-3 + half a bf16 ulp)",
+                "by_rank": [{"global": c[2], "window": c[3]} for c in all_csum]},
             "numa_node": numa,
         }
         if extra:

@@ -136,3 +136,20 @@ def test_block_oracle_matches_torch_definitions():
     hmid = F.gelu(F.layer_norm(x1, (c,), t["norm2_w"], t["norm2_b"], 1e-6) @ t["lin1_w"].T + t["lin1_b"])
     want = (x1 + hmid @ t["lin2_w"].T + t["lin2_b"]).numpy()
     assert np.abs(got - want).max() < 1e-9 * max(1.0, np.abs(want).max())
+
+
+@pytest.mark.parametrize("h,w,bh,hd", [(14, 14, 3, 64), (7, 11, 2, 80), (8, 8, 2, 16)])
+def test_bench_fp32_reference_matches_oracle(h, w, bh, hd):
+    """bench.py's PyTorch fp32 reference (the per-rank sampled parity of the bench line) computes the op the
+    oracle computes: square and non-square grids."""
+    import torch
+    import bench
+    rng = np.random.default_rng(h * w + hd)
+    n = h * w
+    q = rng.standard_normal((bh, n, hd), dtype=np.float32)
+    kt = rng.standard_normal((bh, hd, n), dtype=np.float32)
+    v = rng.standard_normal((bh, n, hd), dtype=np.float32)
+    t = 0.5 * rng.standard_normal((2 * h - 1 + 2 * w - 1, hd), dtype=np.float32)
+    ref = oracle.attention_relpos(q, kt, v, t, h, w, 0.125)
+    got = bench.relpos_attention_fp32(torch, *(torch.from_numpy(x) for x in (q, kt, v, t)), h, w, 0.125).numpy()
+    assert np.abs(got - ref).max() / np.abs(ref).max() < 1e-5
