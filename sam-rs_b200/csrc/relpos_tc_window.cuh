@@ -491,9 +491,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (ui >> 1) & 1;
         // S_t(u) overwrites the tile's columns: the softmax warps must have read O_t(u-1). Tile 1's first S
         // waits for tile 0's first softmax, which sets the two tiles half a step apart: one tile's softmax on
-        // the exp unit then overlaps the other's MMAs and epilogue instead of competing with its softmax.
+        // the exp unit then overlaps the other's MMAs and epilogue instead of competing with its softmax. The
+        // bf16 hd-80 kernel (one-pass softmax) runs the tiles in step instead: there the half-step lag left
+        // tile 0 waiting for the single V stage, which tile 1's P.V of the previous unit still holds (0.407
+        // vs 0.419 ms at bh 12800, faster in each of six interleaved rounds; hd 64 and f16 keep the lag:
+        // 0.180 vs 0.197 ms at hd 64).
+        constexpr bool kInStep = kBf16 && HD == 80;
         okk = wait(&bars->q_full[s], ph) && wait(&bars->k_full[s], ph) &&
-              (ui == 0 ? (t == 0 || wait(&bars->p_full[0], 0)) : wait(&bars->t_free[t], (ui - 1) & 1));
+              (ui == 0 ? (t == 0 || kInStep || wait(&bars->p_full[0], 0)) : wait(&bars->t_free[t], (ui - 1) & 1));
         if (!okk) break;
         tc_fence_after();
 #pragma unroll
