@@ -25,10 +25,11 @@
 // shared memory and written back by one bulk store per warp.
 //
 // Warps: 0 / 1 MMA issuers of query tile 1 / 0 (one warp each, so the two tiles' S -> softmax -> PV ->
-// epilogue chains never wait on each other; tile 1 starts half a step after tile 0), 2-3 kt loaders (thread 0 also issues the q TMA loads, the
-// last thread the v TMA loads; warp 2 allocates TMEM), 4-7 / 8-11 softmax + epilogue of query tile 0 / 1 (thread = query
-// row = TMEM lane); warp 11 covers rows 224..255 only, which are all padding, so it only keeps the
-// barrier counts.
+// epilogue chains never wait on each other; tile 1 starts half a step after tile 0, except in the bf16
+// hd-80 kernel, whose tiles run in step), 2-3 kt loaders (thread 0 also issues the q TMA loads, the last
+// thread the v TMA loads; warp 2 allocates TMEM), 4-7 / 8-11 softmax + epilogue of query tile 0 / 1
+// (thread = query row = TMEM lane); warp 11 covers rows 224..255 only, which are all padding, so it only
+// keeps the barrier counts.
 // TMEM (512 columns): tile t owns [256t, 256t+256): S_t; then P_t (16-bit pairs, cols 0..103) written
 // over the consumed scores; O_t and its row sums accumulate in cols [128, 128+hd+16) once the softmax
 // has consumed S_t (the P.V MMA multiplies by [V | ones]).
