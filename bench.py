@@ -152,17 +152,63 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clock, power and clock-event (throttle) reasons of one GPU, sampled every 10 ms through NVML from a
+    background thread while the timed region runs (nvidia-smi every 200 ms where NVML is unavailable). The GPU
+    is the CUDA device `gpu_index`, matched to its NVML handle by PCI bus id. Reads only; changes nothing."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits, in the order of the names summary() reports
+    REASON_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                   ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.thread = None
+        self.lines = []
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        if torch.cuda.is_available():
+            pr = torch.cuda.get_device_properties(self.gpu)
+            for bus in (f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0",
+                        f"{pr.pci_domain_id:04X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"):
+                try:
+                    return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+                except pynvml.NVMLError:
+                    pass
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def __enter__(self):
+        import threading
+        self.lines = []
+        try:
+            nv, h = self._nvml_handle()
+            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            stop = threading.Event()
+
+            def run():
+                while not stop.is_set():
+                    try:
+                        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                        watts = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    except nv.NVMLError:
+                        break
+                    flags = ["Active" if bits & bit else "Not Active" for _, bit in self.REASON_BITS]
+                    self.lines.append(",".join([str(self.gpu), str(sm), str(smax), f"{watts:.1f}", hex(bits)] + flags))
+                    stop.wait(0.01)
+
+            self._stop = stop
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
@@ -172,6 +218,10 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            return False
         self.lines = []
         if self.proc is not None:
             self.proc.terminate()
@@ -202,10 +252,11 @@ class ClockSampler:
             for name, val in zip(names, f[5:9]):
                 if val.lower() in ("active", "1"):
                     reasons.add(name)
+        how = "nvml every 10 ms" if self.thread is not None else "nvidia-smi every 200 ms"
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": [], "samples": 0, "sampler": how}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm),
-                "power_w": statistics.median(watts) if watts else None}
+                "power_w": statistics.median(watts) if watts else None, "sampler": how}
 
 
 # --------------------------------------------------------------------------------------------
@@ -1187,7 +1238,7 @@ def run_library_context(args):
     """Context for the attention kernels' rooflines: the fused rel-pos kernels against the library's plain
     attention (torch SDPA on its cuDNN backend, no bias at all: less work than the fused op) on the same
     shapes, one GPU. Each is run back to back for `--context-seconds` in alternating phases (ours, library,
-    ours, library) with nvidia-smi sampled during each phase, so that the two are compared at the clocks the
+    ours, library) with the clocks sampled during each phase, so that the two are compared at the clocks the
     power cap leaves each of them. Prints one JSON line ("impl": "library-context")."""
     import torch
     import torch.nn.functional as F
