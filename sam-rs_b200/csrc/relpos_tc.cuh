@@ -88,7 +88,7 @@ inline TcShape tc_select(int h, int w, int hd, const void* q, const void* kt, co
 
 template <typename T, int HD>
 int tc_launch_global(const void* q, const void* kt, const void* v, const void* table, void* out, int64_t bh,
-                     float scale, cudaStream_t st) {
+                     float scale, cudaStream_t st, int num_sms) {
   using namespace tcg;
   constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   if (bh * kN > 0x7fffffffLL || bh * (kN / 256) > 0x7fffffffLL) return 4;
@@ -118,12 +118,15 @@ int tc_launch_global(const void* q, const void* kt, const void* v, const void* t
   ch.exact = !bf16;
   int dev = -1;
   if (bf16 && cudaGetDevice(&dev) == cudaSuccess) ch = global_policy().choose(dev, table, grid, st);
+  const long n_blocks = (long)grid;
   if (ch.exact) {
-    exact<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale, nullptr);
+    exact<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale, nullptr, n_blocks);
     return 0;
   }
-  first<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale, nullptr);
-  fixup<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale, ch.slot);
+  first<<<grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale, nullptr, n_blocks);
+  // the fixup: at most one CTA per SM, each reading its share of the markers and recomputing the marked blocks
+  const unsigned fixup_grid = bf16 && num_sms > 0 && grid > (unsigned)num_sms ? (unsigned)num_sms : grid;
+  fixup<<<fixup_grid, kThreads, smem, st>>>(mq, mk, mv, mt, static_cast<T*>(out), scale, ch.slot, n_blocks);
   global_policy().after_launch(dev, ch, st);
   return 0;
 }
@@ -182,8 +185,8 @@ int tc_launch(TcShape shape, const void* q, const void* kt, const void* v, const
   (void)h;
   (void)w;
   if (shape == TcShape::kGlobal)
-    return hd == 80 ? tc_launch_global<T, 80>(q, kt, v, table, out, bh, scale, st)
-                    : tc_launch_global<T, 64>(q, kt, v, table, out, bh, scale, st);
+    return hd == 80 ? tc_launch_global<T, 80>(q, kt, v, table, out, bh, scale, st, num_sms)
+                    : tc_launch_global<T, 64>(q, kt, v, table, out, bh, scale, st, num_sms);
   if (shape == TcShape::kWindow)
     return hd == 80 ? tc_launch_window<T, 80>(q, kt, v, table, out, bh, scale, st, num_sms)
                     : tc_launch_window<T, 64>(q, kt, v, table, out, bh, scale, st, num_sms);

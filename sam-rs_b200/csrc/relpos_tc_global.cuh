@@ -39,6 +39,8 @@
 #pragma once
 #include <cuda.h>
 
+#include <stddef.h>
+
 #include <type_traits>
 
 #include "common.cuh"
@@ -224,7 +226,7 @@ template <typename T, int HD, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     relpos_attn_global(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmT,
-                       T* __restrict__ out, float scale, unsigned long long* recompute_slot) {
+                       T* __restrict__ out, float scale, unsigned long long* recompute_slot, long n_blocks) {
   using L = Layout<HD>;
   using namespace sm100;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -237,29 +239,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = &bars->abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long bh = blockIdx.x / (kN / 256);
-  const int ct = blockIdx.x % (kN / 256);
+  // One output block (one head x 256 query rows): the speculative and exact launches run one per CTA, the
+  // fixup launch runs the marked ones of its share (below).
+  auto run_block = [&](const long blk) {
+  const long bh = blk / (kN / 256);
+  const int ct = (int)(blk % (kN / 256));
   const int row0 = ct * 256;  // first query row of the CTA
   const int I0 = ct * 4;      // its first grid row
   T* const marker = out + (bh * kN + row0) * HD;  // first element of the CTA's output block
-  {
-    // The whole CTA leaves here or none of it does (thread 0 decides; the barriers, TMEM and the warp
-    // roles below need every warp): after an earlier CTA reported a fault, and in the fixup launch for the
-    // CTAs whose speculative pass did not leave the NaN marker.
-    int skip = 0;
-    if (threadIdx.x == 0) {
-      skip = device_faulted();
-      if constexpr (MODE == kModeFixup) {
-        const float m = to_f(*reinterpret_cast<volatile T*>(marker));
-        skip |= !(m != m);
-        if (!skip) {
-          atomicAdd(&g_recomputed, 1ull);
-          if (recompute_slot) atomicAdd(recompute_slot, 1ull);  // the host's per-layer measurement
-        }
-      }
-    }
-    if (__syncthreads_or(skip)) return;
-  }
+  // The whole CTA leaves here or none of it does (thread 0 decides; the barriers, TMEM and the warp roles
+  // below need every warp): after an earlier CTA reported a fault.
+  if (__syncthreads_or(threadIdx.x == 0 && device_faulted())) return;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -299,7 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 2) {
     tmem_alloc(&bars->tmem_base, 512);
-    tmem_relinquish();
+    // the fixup launch allocates again for its CTA's next block, so it keeps the permit
+    if constexpr (MODE != kModeFixup) tmem_relinquish();
   }
   {
     // the ones block of every V stage (the TMA loads never write it); read by the MMA (async proxy)
@@ -316,14 +307,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   if (warp < 4) {
-    regs_dec<kRegsLow>();
+    // (the fixup launch runs several blocks per CTA and keeps the launch's even split: its blocks are rare)
+    if constexpr (MODE != kModeFixup) regs_dec<kRegsLow>();
     if (warp == 0) {
       // ---------------------------------------------------------------- TMA producer
       // (Q and the tables went out with the barrier set-up) K and V of every key tile
       int issued_k = 0, issued_v = 0;
       if (lane == 0) {
         // test hook: CTA 0 never loads this key tile (-1: none), so the MMA issuer's wait for it runs out
-        const int withhold = blockIdx.x == 0 ? *reinterpret_cast<volatile int*>(&g_withhold_key_tile) : -1;
+        const int withhold = blk == 0 ? *reinterpret_cast<volatile int*>(&g_withhold_key_tile) : -1;
         for (int j = 0; j < kNT; ++j) {
           const int jj = j, st = jj % kStages;
           const uint32_t prev = ((jj / kStages) - 1) & 1;
@@ -450,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    regs_inc<kRegsHigh>();
+    if constexpr (MODE != kModeFixup) regs_inc<kRegsHigh>();
     // ------------------------------------------------------------------ softmax warps
     const int sw = warp - 4;
     const int q = sw >> 3;                // query tile
@@ -736,6 +728,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+  if constexpr (MODE == kModeFixup) {
+    // the barriers are initialised again for the CTA's next block
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint64_t* b = reinterpret_cast<uint64_t*>(bars);
+      for (int i = 0; i < (int)(offsetof(Bars, tmem_base) / sizeof(uint64_t)); ++i) mbar_inval(b + i);
+    }
+    __syncthreads();
+  }
+  };
+
+  if constexpr (MODE == kModeFixup) {
+    // The fixup launch: a grid of at most one CTA per SM; CTA b owns the blocks b, b + grid, b + 2 grid, ...
+    // Its threads read those blocks' markers at once (640 per round), and the CTA runs the exact pass of
+    // the marked ones only. With nothing marked a launch is one round of marker reads per CTA.
+    __shared__ int fx_count;
+    __shared__ int fx_list[kThreads];
+    for (long k0 = 0; blockIdx.x + k0 * (long)gridDim.x < n_blocks; k0 += kThreads) {
+      if (threadIdx.x == 0) fx_count = 0;
+      __syncthreads();
+      const long cand = blockIdx.x + (k0 + threadIdx.x) * (long)gridDim.x;
+      if (cand < n_blocks && !device_faulted()) {
+        const T* m = out + ((cand / (kN / 256)) * kN + (cand % (kN / 256)) * 256) * HD;
+        const float v = to_f(*reinterpret_cast<const volatile T*>(m));
+        if (v != v) {
+          fx_list[atomicAdd(&fx_count, 1)] = threadIdx.x;
+          atomicAdd(&g_recomputed, 1ull);
+          if (recompute_slot) atomicAdd(recompute_slot, 1ull);  // the host's per-layer measurement
+        }
+      }
+      __syncthreads();
+      const int n = fx_count;
+      for (int i = 0; i < n; ++i) run_block(blockIdx.x + (k0 + fx_list[i]) * (long)gridDim.x);
+      __syncthreads();
+    }
+  } else {
+    (void)n_blocks;
+    run_block(blockIdx.x);
   }
 }
 
