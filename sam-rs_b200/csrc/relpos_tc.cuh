@@ -99,7 +99,7 @@ int tc_launch_global(const void* q, const void* kt, const void* v, const void* t
   if (!rc) rc = make_map(&mt, bf16, table, HD, 4 * kSide - 2, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
   // f16: the exact kernel. bf16: the speculative kernel, then the fixup launch, which recomputes exactly
-  // the CTAs the first one marked (the others return at once); or, for a layer whose measured recompute
+  // the blocks the first one marked (one CTA per SM scans the markers); or, for a layer whose measured recompute
   // share made the speculative pass the slower choice (global_policy.h), the exact kernel alone.
   auto exact = relpos_attn_global<T, HD, kModeExact>;
   auto first = relpos_attn_global<T, HD, bf16 ? kModeSpec : kModeExact>;

@@ -65,8 +65,9 @@ constexpr float kRescaleThreshold = 8.f;  // log2 units
 constexpr float kSpecCap = 96.f, kSpecLimit = 112.f;
 constexpr float kSpecSumLimit = 0x1p112f;  // 2^kSpecLimit
 // Kernel modes: the exact two-pass softmax (f16); the speculative pass (bf16), which marks a CTA that needs
-// the exact pass by a NaN in the first element of its output block; the exact pass of the marked CTAs
-// only (bf16, launched right after the speculative one; the others return at once).
+// the exact pass by a NaN in the first element of its output block; the exact pass of the marked blocks
+// only (bf16, launched right after the speculative one with at most one CTA per SM, each scanning its share
+// of the markers).
 constexpr int kModeExact = 0, kModeSpec = 1, kModeFixup = 2;
 
 template <int HD>
