@@ -248,6 +248,33 @@ def test_global_bf16_overflow_recompute(samrs, cuda, hd):
     assert err < HALF_TOL, err
 
 
+def test_global_bf16_fixup_several_blocks_per_cta(samrs, cuda):
+    """The bf16 fixup launch runs at most one CTA per SM, each recomputing every marked block of its share in
+    turn: 24 heads x 16 blocks = 384 blocks, all marked (a key in a late tile jumps ~26 log2 units above the
+    running max of every row and v ~ 1e35, so every single-pass block overflows), i.e. two or three blocks per
+    CTA. Every block is counted once, and sampled heads match the oracle."""
+    h = w = 64
+    hd, bh = 80, 24
+    q, kt, v, t = make_inputs(h, w, bh, hd, seed=31, table_std=0.5)
+    q[:, :, 0] = 4.0
+    v *= 1e35
+    for b in range(bh):
+        kt[b, 0, 128 * (20 + b % 12) + 7 * b % 128] = 40.0
+    scale = hd ** -0.5
+    qd, ktd, vd, td = (to_dev(x, "bf16", cuda) for x in (q, kt, v, t))
+    samrs.global_policy(td, reset=True)
+    samrs.recompute_count(clear=True)
+    out = samrs.attention_relpos(qd, ktd, vd, td, h, w, scale)
+    assert samrs.recompute_count(clear=True) == bh * 16
+    assert samrs.device_status() == 0
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    heads = [0, 7, 16, 23]
+    ref = oracle.attention_relpos(rounded(qd[heads]), rounded(ktd[heads]), rounded(vd[heads]), rounded(td), h, w, scale)
+    err = parity_err(got[heads], ref, "bf16")
+    assert err < HALF_TOL, err
+
+
 def test_bf16_recompute_counter(samrs, cuda):
     """The recompute counter: random N(0,1) activations and N(0,0.5) tables need no exact second pass; the
     overflow case above marks some CTAs (one head x 256 rows each) and the counter sees them."""
