@@ -743,8 +743,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if constexpr (MODE == kModeFixup) {
     // The fixup launch: a grid of at most one CTA per SM; CTA b owns the blocks b, b + grid, b + 2 grid, ...
-    // Its threads read those blocks' markers at once (640 per round), and the CTA runs the exact pass of
-    // the marked ones only. With nothing marked a launch is one round of marker reads per CTA.
+    // Its threads read those blocks' markers at once (640 at a time), and the CTA runs the exact pass of
+    // the marked ones only. With nothing marked a launch is one pass of marker reads per CTA.
     __shared__ int fx_count;
     __shared__ int fx_list[kThreads];
     for (long k0 = 0; blockIdx.x + k0 * (long)gridDim.x < n_blocks; k0 += kThreads) {
