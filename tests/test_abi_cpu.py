@@ -127,3 +127,39 @@ def test_linear_and_norm_empty_and_null():
     assert a.lib().samrs_qkv_linear_window_fwd(0, 0, 0, 0, 0, 64, 64, 14, 12, 64, 1, None) == 0
     assert a.lib().samrs_qkv_linear_window_fwd(0, 0, 0, 0, 1, 64, 64, 14, 12, 12, 1, None) == -2  # hd % 16
     assert a.lib().samrs_qkv_linear_window_fwd(0, 0, 0, 0, 1, 64, 64, 14, 12, 64, 1, None) == -1  # null
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """include/samrs_b200.h is a C header (what the reference's Rust FFI, or any C caller, binds): a C99 program
+    that includes it compiles with gcc, links against the library and gets the error codes and messages of the
+    argument checks (no GPU needed for those)."""
+    import os
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    lib_dir = os.path.join(root, "sam-rs_b200")
+    src = tmp_path / "probe.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "samrs_b200.h"
+int main(void) {
+  if (samrs_abi_version() != SAMRS_ABI_VERSION) return 1;
+  int rc = samrs_relpos_attn_fwd(0, 0, 0, 0, 0, 1, 4, 4, 8, 0.5f, 7, 0);
+  if (rc != SAMRS_ERR_INVALID || strlen(samrs_last_error()) == 0) return 2;
+  rc = samrs_relpos_attn_fwd_ex(0, 0, 0, 0, 0, 1, 0, 4, 8, 0.5f, SAMRS_F32, SAMRS_IMPL_AUTO, 0);
+  if (rc != SAMRS_ERR_UNSUPPORTED) return 3;
+  rc = samrs_linear_fwd(0, 0, 0, 0, 0, 4, 16, 8, 9, SAMRS_BF16, 0);
+  if (rc != SAMRS_ERR_INVALID) return 4;
+  printf("%s\n", samrs_last_error());
+  return 0;
+}
+''')
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(root, "include"), str(src), "-o", str(exe),
+                    "-L", lib_dir, "-lsamrs_b200", f"-Wl,-rpath,{lib_dir}"], check=True, timeout=120)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+    assert "epilogue" in r.stdout
